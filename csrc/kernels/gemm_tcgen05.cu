@@ -1,0 +1,370 @@
+// Persistent warp-specialized bf16 GEMM for sm_100a on the 5th-generation
+// tensor cores:  C[M,N] (op)= alpha * sum_k A[m,k] * B[n,k].
+//
+//   warp 0      TMA producer: 128B-swizzled A/B tiles into a STAGES-deep ring
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 2..5  epilogue: tcgen05.ld from TMEM, fused elementwise op, store
+//
+// The fp32 accumulator of a 128 x BN tile lives in tensor memory; two
+// accumulator buffers let the epilogue of tile i overlap the MMAs of tile i+1.
+// Operands may be K-major or MN-major, which covers the forward pass
+// (X W^T), the data gradient (dY W) and the weight gradient (dY^T X) without
+// any transposed copies. Split-K (with fp32 vector atomics in the epilogue)
+// keeps all 148 SMs busy on the skinny weight-gradient GEMMs.
+//
+// Replaces the reference's cuBLAS matmuls at rs-nanogpt src/model/linear.rs:46-49
+// (Q/K/V/c_proj/c_fc/mlp.c_proj/lm_head) and folds in the ReLU^2 of
+// src/model/mlp.rs:32-33 and the residual adds of src/model/block.rs:55-58.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+#include "status.h"
+#include "tma_host.h"
+
+namespace nk {
+
+enum GemmMode : int {
+  kStoreBf16 = 0,   // C = alpha*acc
+  kRelu2 = 1,       // C = relu(alpha*acc)^2, AUX_OUT = alpha*acc
+  kDRelu2 = 2,      // C = alpha*acc * 2*relu(AUX)
+  kResidual = 3,    // C = alpha*acc + AUX (AUX may alias C)
+  kAtomicF32 = 4,   // C(fp32) += alpha*acc   (split-K capable)
+};
+
+struct GemmArgs {
+  int M, N, K;
+  int num_m, num_n, splits, kb_per_split, kb_total;
+  int a_mn_major, b_mn_major;
+  int mode;
+  float alpha;
+  void* C;
+  long ldc;
+  const __nv_bfloat16* aux;
+  long ld_aux;
+  __nv_bfloat16* aux_out;
+  long ld_aux_out;
+  int* err;
+};
+
+constexpr int BM = 128, BK = 64, kGroupM = 16;
+
+template <int BN>
+struct Smem {
+  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTotal = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+// Work unit -> (tile row m, tile col n, k-block range). Tiles are rastered in
+// groups of kGroupM row-blocks so concurrently running CTAs share B tiles in L2.
+__device__ __forceinline__ void unit_coords(const GemmArgs& a, int u, int& m, int& n, int& kb0, int& kb1) {
+  const int tiles = a.num_m * a.num_n;
+  const int tile = u % tiles, split = u / tiles;
+  const int per_group = kGroupM * a.num_n;
+  const int group = tile / per_group;
+  const int first_m = group * kGroupM;
+  const int gsz = min(a.num_m - first_m, kGroupM);
+  const int r = tile % per_group;
+  m = first_m + r % gsz;
+  n = r / gsz;
+  kb0 = split * a.kb_per_split;
+  kb1 = min(a.kb_total, kb0 + a.kb_per_split);
+}
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* p, const float (&x)[32]) {
+  uint4* q = reinterpret_cast<uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    q[i] = make_uint4(pack_bf16x2(x[8 * i], x[8 * i + 1]), pack_bf16x2(x[8 * i + 2], x[8 * i + 3]),
+                      pack_bf16x2(x[8 * i + 4], x[8 * i + 5]), pack_bf16x2(x[8 * i + 6], x[8 * i + 7]));
+}
+
+__device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int row, int col0, const float (&v)[32]) {
+  if (row >= a.M) return;
+  const bool full = col0 + 32 <= a.N;
+  if (a.mode == kAtomicF32) {
+    float* c = reinterpret_cast<float*>(a.C) + long(row) * a.ldc + col0;
+    if (full) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        atomicAdd(reinterpret_cast<float4*>(c + i), make_float4(a.alpha * v[i], a.alpha * v[i + 1],
+                                                                a.alpha * v[i + 2], a.alpha * v[i + 3]));
+    } else {
+      for (int i = 0; i < 32 && col0 + i < a.N; ++i) atomicAdd(c + i, a.alpha * v[i]);
+    }
+    return;
+  }
+  __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(a.C) + long(row) * a.ldc + col0;
+  float x[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) x[i] = a.alpha * v[i];
+  if (a.mode == kRelu2) {
+    __nv_bfloat16* h = a.aux_out + long(row) * a.ld_aux_out + col0;
+    if (full) store_bf16x32(h, x);
+    else
+      for (int i = 0; i < 32 && col0 + i < a.N; ++i) h[i] = __float2bfloat16(x[i]);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      // Square the bf16-rounded pre-activation, as relu(h)^2 on a bf16 h would.
+      float hr = fmaxf(__bfloat162float(__float2bfloat16(x[i])), 0.f);
+      x[i] = hr * hr;
+    }
+  } else if (a.mode == kDRelu2 || a.mode == kResidual) {
+    const __nv_bfloat16* s = a.aux + long(row) * a.ld_aux + col0;
+    float y[32];
+    if (full) {
+      const uint4* sp = reinterpret_cast<const uint4*>(s);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint4 w = sp[i];
+        uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float2 f = unpack_bf16x2(ws[j]);
+          y[8 * i + 2 * j] = f.x;
+          y[8 * i + 2 * j + 1] = f.y;
+        }
+      }
+    } else {
+      for (int i = 0; i < 32; ++i) y[i] = col0 + i < a.N ? __bfloat162float(s[i]) : 0.f;
+    }
+    if (a.mode == kDRelu2) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        // d/dh relu(h)^2 = 2 relu(h), applied to the bf16-rounded upstream grad.
+        float g = __bfloat162float(__float2bfloat16(x[i]));
+        x[i] = g * 2.f * fmaxf(y[i], 0.f);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) x[i] = __bfloat162float(__float2bfloat16(x[i])) + y[i];
+    }
+  }
+  if (full) store_bf16x32(c, x);
+  else
+    for (int i = 0; i < 32 && col0 + i < a.N; ++i) c[i] = __float2bfloat16(x[i]);
+}
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const GemmArgs args) {
+  using S = Smem<BN>;
+  constexpr int STAGES = S::kStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * S::kStageBytes);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* acc_full = empty_bar + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int units = args.num_m * args.num_n * args.splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
+    for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 4); }
+    fence_barrier_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        int m, n, kb0, kb1;
+        unit_coords(args, u, m, n, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, kErrTimeoutProducer, args.err)) { ok = false; break; }
+          uint8_t* sa = smem + stage * S::kStageBytes;
+          uint8_t* sb = sa + S::kABytes;
+          mbar_arrive_expect_tx(&full_bar[stage], S::kStageBytes);
+          if (!args.a_mn_major) {
+            tma_load_2d(sa, &tmA, &full_bar[stage], kb * BK, m * BM);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_2d(sa + j * 8192, &tmA, &full_bar[stage], m * BM + 64 * j, kb * BK);
+          }
+          if (!args.b_mn_major) {
+            tma_load_2d(sb, &tmB, &full_bar[stage], kb * BK, n * BN);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 8192, &tmB, &full_bar[stage], n * BN + 64 * j, kb * BK);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16(BM, BN, args.a_mn_major, args.b_mn_major);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++local) {
+        int m, n, kb0, kb1;
+        unit_coords(args, u, m, n, kb0, kb1);
+        const int b = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&acc_empty[b], acc_phase ^ 1, kErrTimeoutMma, args.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + b * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, kErrTimeoutMma, args.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * S::kStageBytes);
+          const uint32_t sb = sa + S::kABytes;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = args.a_mn_major ? sw128_desc(sa + k * 2048, 8192, 1024)
+                                                : sw128_desc(sa + k * 32, 16, 1024);
+            const uint64_t bd = args.b_mn_major ? sw128_desc(sb + k * 2048, 8192, 1024)
+                                                : sw128_desc(sb + k * 32, 16, 1024);
+            umma_bf16(d_tmem, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        umma_commit(&acc_full[b]);
+      }
+    }
+  } else {
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int local = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+      int m, n, kb0, kb1;
+      unit_coords(args, u, m, n, kb0, kb1);
+      const int b = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&acc_full[b], acc_phase, kErrTimeoutEpilogue, args.err)) break;
+      tc_fence_after();
+      const int row = m * BM + q * 32 + lane;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        tmem_ld_32x32(tmem_base + (uint32_t(q * 32) << 16) + b * BN + c * 32, v);
+        const int col0 = n * BN + c * 32;
+        if (col0 < args.N) epilogue_chunk(args, row, col0, v);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+static int num_sms() {
+  static int n = [] {
+    int dev, v;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    return v;
+  }();
+  return n;
+}
+
+template <int BN>
+static void launch(const GemmArgs& args, const CUtensorMap& ta, const CUtensorMap& tb, cudaStream_t stream) {
+  static bool configured = false;
+  if (!configured) {
+    TORCH_CHECK(cudaFuncSetAttribute(gemm_bf16_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Smem<BN>::kTotal) == cudaSuccess,
+                "gemm: cannot reserve shared memory");
+    configured = true;
+  }
+  const int units = args.num_m * args.num_n * args.splits;
+  const int grid = std::min(units, num_sms());
+  gemm_bf16_kernel<BN><<<grid, 192, Smem<BN>::kTotal, stream>>>(ta, tb, args);
+  TORCH_CHECK(cudaGetLastError() == cudaSuccess, "gemm launch failed");
+}
+
+static void check_bf16_2d(const torch::Tensor& t, int64_t rows, int64_t cols, const char* what) {
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16 && t.dim() == 2 && t.size(0) == rows && t.size(1) == cols &&
+                  t.stride(1) == 1 && (t.stride(0) * 2) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
+              "gemm: bad ", what);
+}
+
+// C (op)= alpha * A . B^T with operand layouts:
+//   A: a_mn_major ? [K, M] : [M, K]      B: b_mn_major ? [K, N] : [N, K]
+void gemm(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_major, torch::Tensor C, int64_t mode,
+          double alpha, c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> aux_out, int64_t splits,
+          int64_t block_n) {
+  TORCH_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda(), "gemm: CUDA tensors required");
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm: bf16 operands");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "gemm: 2-D tensors");
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && C.stride(1) == 1, "gemm: row-major tensors");
+  const int M = int(a_mn_major ? A.size(1) : A.size(0));
+  const int K = int(a_mn_major ? A.size(0) : A.size(1));
+  const int N = int(b_mn_major ? B.size(1) : B.size(0));
+  TORCH_CHECK((b_mn_major ? B.size(0) : B.size(1)) == K, "gemm: K mismatch");
+  TORCH_CHECK(C.size(0) == M && C.size(1) == N, "gemm: C shape mismatch");
+  TORCH_CHECK(M > 0 && N > 0 && K > 0, "gemm: empty problem");
+  const bool f32out = mode == kAtomicF32;
+  TORCH_CHECK(C.scalar_type() == (f32out ? at::kFloat : at::kBFloat16), "gemm: C dtype does not fit the mode");
+  TORCH_CHECK(splits == 1 || f32out, "gemm: split-K needs the atomic fp32 mode");
+  const int elt = f32out ? 4 : 2;
+  TORCH_CHECK((C.stride(0) * elt) % 16 == 0 && reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0,
+              "gemm: C rows must be 16-byte aligned");
+
+  GemmArgs args{};
+  args.M = M; args.N = N; args.K = K;
+  args.a_mn_major = a_mn_major; args.b_mn_major = b_mn_major;
+  args.mode = int(mode);
+  args.alpha = float(alpha);
+  args.C = C.data_ptr();
+  args.ldc = C.stride(0);
+  args.err = error_word();
+  if (mode == kDRelu2 || mode == kResidual) {
+    TORCH_CHECK(aux.has_value(), "gemm: mode needs aux");
+    check_bf16_2d(*aux, M, N, "aux");
+    args.aux = reinterpret_cast<const __nv_bfloat16*>(aux->data_ptr());
+    args.ld_aux = aux->stride(0);
+  }
+  if (mode == kRelu2) {
+    TORCH_CHECK(aux_out.has_value(), "gemm: relu2 needs aux_out");
+    check_bf16_2d(*aux_out, M, N, "aux_out");
+    args.aux_out = reinterpret_cast<__nv_bfloat16*>(aux_out->data_ptr());
+    args.ld_aux_out = aux_out->stride(0);
+  }
+  const int BN = block_n == 128 ? 128 : 256;
+  args.num_m = (M + BM - 1) / BM;
+  args.num_n = (N + BN - 1) / BN;
+  args.kb_total = (K + BK - 1) / BK;
+  int s = int(std::max<int64_t>(1, std::min<int64_t>(splits, args.kb_total)));
+  args.kb_per_split = (args.kb_total + s - 1) / s;
+  args.splits = (args.kb_total + args.kb_per_split - 1) / args.kb_per_split;
+
+  // Tensor maps: inner dimension first. K-major boxes are 64 (K) x rows;
+  // MN-major boxes are 64 (MN) x 64 (K), issued BM/64 or BN/64 times per stage.
+  CUtensorMap ta = a_mn_major ? make_tmap_bf16_2d(A.data_ptr(), M, K, A.stride(0), 64, 64)
+                              : make_tmap_bf16_2d(A.data_ptr(), K, M, A.stride(0), 64, BM);
+  CUtensorMap tb = b_mn_major ? make_tmap_bf16_2d(B.data_ptr(), N, K, B.stride(0), 64, 64)
+                              : make_tmap_bf16_2d(B.data_ptr(), K, N, B.stride(0), 64, BN);
+  const at::cuda::CUDAGuard guard(A.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  if (BN == 128) launch<128>(args, ta, tb, stream);
+  else launch<256>(args, ta, tb, stream);
+}
+
+}  // namespace nk

@@ -1,0 +1,86 @@
+"""tcgen05 GEMM entry points (kernel: ``csrc/kernels/gemm_tcgen05.cu``).
+
+All functions compute ``C (op)= alpha * A @ B^T`` with bf16 operands and fp32
+accumulation in tensor memory, choosing operand majorness so no transposed
+copies are ever made:
+
+* ``linear(x, w)``            y = x w^T         (forward, both K-major)
+* ``linear_dgrad(dy, w)``     dx = dy w         (w is MN-major)
+* ``linear_wgrad(dy, x, g)``  g += dy^T x       (both MN-major, split-K, fp32 atomics)
+"""
+import torch
+
+from ._ext import ext
+
+STORE, RELU2, DRELU2, RESIDUAL, ATOMIC_F32 = 0, 1, 2, 3, 4
+_NUM_SMS = None
+
+
+def _sms() -> int:
+    global _NUM_SMS
+    if _NUM_SMS is None:
+        _NUM_SMS = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    return _NUM_SMS
+
+
+def _block_n(n: int) -> int:
+    return 256 if n >= 256 and n % 256 == 0 else 128
+
+
+def linear(x, w, out=None, alpha: float = 1.0):
+    """out[M,N] = alpha * x[M,K] @ w[N,K]^T (bf16)."""
+    if out is None:
+        out = torch.empty(x.shape[0], w.shape[0], device=x.device, dtype=torch.bfloat16)
+    ext().gemm(x, False, w, False, out, STORE, alpha, None, None, 1, _block_n(w.shape[0]))
+    return out
+
+
+def linear_relu2(x, w, act=None, h=None):
+    """(act, h): h = x w^T and act = relu(h)^2, both bf16, in one GEMM."""
+    m, n = x.shape[0], w.shape[0]
+    if act is None:
+        act = torch.empty(m, n, device=x.device, dtype=torch.bfloat16)
+    if h is None:
+        h = torch.empty_like(act)
+    ext().gemm(x, False, w, False, act, RELU2, 1.0, None, h, 1, _block_n(n))
+    return act, h
+
+
+def linear_residual(x, w, residual, out=None):
+    """out = residual + x w^T (out may be `residual` itself)."""
+    if out is None:
+        out = torch.empty_like(residual)
+    ext().gemm(x, False, w, False, out, RESIDUAL, 1.0, residual, None, 1, _block_n(w.shape[0]))
+    return out
+
+
+def linear_dgrad(dy, w, out=None, alpha: float = 1.0):
+    """dx[M,K] = alpha * dy[M,N] @ w[N,K]."""
+    if out is None:
+        out = torch.empty(dy.shape[0], w.shape[1], device=dy.device, dtype=torch.bfloat16)
+    ext().gemm(dy, False, w, True, out, STORE, alpha, None, None, 1, _block_n(w.shape[1]))
+    return out
+
+
+def linear_dgrad_drelu2(dy, w, h, out=None):
+    """dh = (dy @ w) * 2 relu(h): the data gradient through a ReLU^2 MLP input."""
+    if out is None:
+        out = torch.empty(dy.shape[0], w.shape[1], device=dy.device, dtype=torch.bfloat16)
+    ext().gemm(dy, False, w, True, out, DRELU2, 1.0, h, None, 1, _block_n(w.shape[1]))
+    return out
+
+
+def linear_wgrad(dy, x, grad, alpha: float = 1.0, splits: int = 0):
+    """grad[N,K] (fp32) += alpha * dy[M,N]^T @ x[M,K].
+
+    The contraction runs over the M tokens; it is split across CTAs so the
+    small output still fills every SM, and partial tiles meet in fp32 atomics.
+    """
+    n, k = grad.shape
+    bn = _block_n(k)
+    if splits <= 0:
+        tiles = ((n + 127) // 128) * ((k + bn - 1) // bn)
+        k_blocks = (dy.shape[0] + 63) // 64
+        splits = max(1, min(k_blocks // 8, (8 * _sms() + tiles - 1) // tiles))
+    ext().gemm(dy, True, x, True, grad, ATOMIC_F32, alpha, None, None, splits, bn)
+    return grad
