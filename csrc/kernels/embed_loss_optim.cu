@@ -1,0 +1,283 @@
+// Memory-bound kernels around the GEMMs:
+//   * embedding_fwd/bwd  gather fp32 master rows -> bf16 activations; scatter-add
+//                        bf16 row grads into the fp32 gradient with vector atomics
+//                        (rs-nanogpt src/model/embedding.rs:33-35, src/model/gpt.rs:103)
+//   * softmax_xent       one pass over a chunk of bf16 logits rows: fp32 log-sum-exp,
+//                        per-row NLL with ignore_index -1, and (optionally) the
+//                        gradient (softmax - onehot) * scale written in place over
+//                        the logits (src/model/loss.rs:20-82). Together with the
+//                        tcgen05 GEMMs this is the fused lm_head + cross-entropy:
+//                        the full (B*T, V) logits are never materialized.
+//   * adamw_step         candle AdamW semantics (decoupled decay, bias correction)
+//                        on a contiguous slice of the flat master/grad/m/v buffers,
+//                        also refreshing the bf16 working copy (src/train/optim.rs)
+//   * sumsq              sum of squares for the gradient norm
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace nk {
+
+// ---- embedding --------------------------------------------------------------
+
+__global__ void embedding_fwd_kernel(const int64_t* __restrict__ idx, const float* __restrict__ wte,
+                                     __nv_bfloat16* __restrict__ out, int rows, int C, int V) {
+  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (row >= rows) return;
+  const int64_t t = idx[row];
+  if (t < 0 || t >= V) return;  // host validates ids; never read out of range
+  const float4* src = reinterpret_cast<const float4*>(wte + t * C);
+  uint2* dst = reinterpret_cast<uint2*>(out + long(row) * C);
+  for (int c = lane; c < C / 4; c += 32) {
+    float4 f = src[c];
+    dst[c] = make_uint2(pack_bf16x2(f.x, f.y), pack_bf16x2(f.z, f.w));
+  }
+}
+
+__global__ void embedding_bwd_kernel(const int64_t* __restrict__ idx, const __nv_bfloat16* __restrict__ dx,
+                                     float* __restrict__ grad, int rows, int C, int V) {
+  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (row >= rows) return;
+  const int64_t t = idx[row];
+  if (t < 0 || t >= V) return;
+  const uint2* src = reinterpret_cast<const uint2*>(dx + long(row) * C);
+  float4* dst = reinterpret_cast<float4*>(grad + t * C);
+  for (int c = lane; c < C / 4; c += 32) {
+    uint2 w = src[c];
+    float2 a = unpack_bf16x2(w.x), b = unpack_bf16x2(w.y);
+    atomicAdd(dst + c, make_float4(a.x, a.y, b.x, b.y));
+  }
+}
+
+void embedding_fwd(torch::Tensor idx, torch::Tensor wte, torch::Tensor out) {
+  TORCH_CHECK(idx.scalar_type() == at::kLong && idx.is_contiguous(), "embedding: int64 ids");
+  TORCH_CHECK(wte.scalar_type() == at::kFloat && wte.is_contiguous() && out.is_contiguous(), "embedding: layout");
+  const int rows = int(idx.numel()), V = int(wte.size(0)), C = int(wte.size(1));
+  TORCH_CHECK(C % 4 == 0 && out.numel() == int64_t(rows) * C, "embedding: shape");
+  const at::cuda::CUDAGuard guard(idx.device());
+  const int warps = 8;
+  embedding_fwd_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      idx.data_ptr<int64_t>(), wte.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rows, C, V);
+  TORCH_CHECK(cudaGetLastError() == cudaSuccess, "embedding_fwd launch failed");
+}
+
+void embedding_bwd(torch::Tensor idx, torch::Tensor dx, torch::Tensor grad) {
+  TORCH_CHECK(idx.scalar_type() == at::kLong && idx.is_contiguous() && dx.is_contiguous(), "embedding_bwd: layout");
+  TORCH_CHECK(grad.scalar_type() == at::kFloat && grad.is_contiguous(), "embedding_bwd: fp32 grad");
+  const int rows = int(idx.numel()), V = int(grad.size(0)), C = int(grad.size(1));
+  const at::cuda::CUDAGuard guard(idx.device());
+  const int warps = 8;
+  embedding_bwd_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      idx.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(dx.data_ptr()), grad.data_ptr<float>(), rows, C,
+      V);
+  TORCH_CHECK(cudaGetLastError() == cudaSuccess, "embedding_bwd launch failed");
+}
+
+// ---- softmax cross-entropy over a logits chunk ---------------------------------
+
+constexpr int kXentThreads = 512;
+
+template <typename Op>
+__device__ __forceinline__ float block_reduce(float v, float* smem, Op op) {
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if (lane == 0) smem[warp] = v;
+  __syncthreads();
+  v = smem[0];
+  for (int w = 1; w < kXentThreads / 32; ++w) v = op(v, smem[w]);
+  return v;
+}
+
+// NV = 8-element vectors held in registers per thread (NV * 8 * 512 >= V).
+template <int NV>
+__global__ void __launch_bounds__(kXentThreads) softmax_xent_kernel(
+    __nv_bfloat16* logits, long ld, const int64_t* __restrict__ targets, float* __restrict__ nll_out, int V,
+    float grad_scale, bool write_grad) {
+  __shared__ float red[kXentThreads / 32];
+  const int row = blockIdx.x;
+  __nv_bfloat16* lr = logits + long(row) * ld;
+  uint4 reg[NV];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * kXentThreads + threadIdx.x) * 8;
+    if (c < V) {
+      reg[i] = *reinterpret_cast<const uint4*>(lr + c);
+      uint32_t w[4] = {reg[i].x, reg[i].y, reg[i].z, reg[i].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = unpack_bf16x2(w[j]);
+        mx = fmaxf(mx, fmaxf(f.x, f.y));
+      }
+    }
+  }
+  mx = block_reduce(mx, red, [](float a, float b) { return fmaxf(a, b); });
+  float se = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * kXentThreads + threadIdx.x) * 8;
+    if (c < V) {
+      uint32_t w[4] = {reg[i].x, reg[i].y, reg[i].z, reg[i].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = unpack_bf16x2(w[j]);
+        se += __expf(f.x - mx) + __expf(f.y - mx);
+      }
+    }
+  }
+  se = block_reduce(se, red, [](float a, float b) { return a + b; });
+  const float lse = mx + __logf(se);
+  const int64_t t = targets[row];
+  const bool valid = t >= 0 && t < V;
+  if (threadIdx.x == 0 && nll_out) nll_out[row] = valid ? lse - __bfloat162float(lr[t]) : 0.f;
+  if (!write_grad) return;
+  __syncthreads();  // lr[t] read above before it is overwritten
+  const float s = valid ? grad_scale : 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * kXentThreads + threadIdx.x) * 8;
+    if (c < V) {
+      uint32_t w[4] = {reg[i].x, reg[i].y, reg[i].z, reg[i].w};
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = unpack_bf16x2(w[j]);
+        const int col = c + 2 * j;
+        float g0 = __expf(f.x - lse) - (col == t ? 1.f : 0.f);
+        float g1 = __expf(f.y - lse) - (col + 1 == t ? 1.f : 0.f);
+        o[j] = pack_bf16x2(g0 * s, g1 * s);
+      }
+      *reinterpret_cast<uint4*>(lr + c) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+// logits: (rows, V) bf16 chunk; targets: (rows,) int64 with -1 = ignore.
+// nll (optional): (rows,) fp32 per-row loss (0 where ignored).
+void softmax_xent(torch::Tensor logits, torch::Tensor targets, c10::optional<torch::Tensor> nll, double grad_scale,
+                  bool write_grad) {
+  TORCH_CHECK(logits.scalar_type() == at::kBFloat16 && logits.dim() == 2 && logits.stride(1) == 1, "xent: logits");
+  TORCH_CHECK(targets.scalar_type() == at::kLong && targets.is_contiguous(), "xent: int64 targets");
+  const int rows = int(logits.size(0)), V = int(logits.size(1));
+  TORCH_CHECK(targets.numel() == rows, "xent: targets length");
+  TORCH_CHECK(V % 8 == 0 && logits.stride(0) % 8 == 0, "xent: V and row stride must be multiples of 8");
+  float* np = nullptr;
+  if (nll.has_value()) {
+    TORCH_CHECK(nll->scalar_type() == at::kFloat && nll->numel() == rows, "xent: nll");
+    np = nll->data_ptr<float>();
+  }
+  const at::cuda::CUDAGuard guard(logits.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto lp = reinterpret_cast<__nv_bfloat16*>(logits.data_ptr());
+  const int per = kXentThreads * 8;
+  const int nv = (V + per - 1) / per;
+#define XENT(N) softmax_xent_kernel<N><<<rows, kXentThreads, 0, stream>>>(lp, logits.stride(0), \
+      targets.data_ptr<int64_t>(), np, V, float(grad_scale), write_grad)
+  if (nv <= 1) XENT(1);
+  else if (nv <= 2) XENT(2);
+  else if (nv <= 4) XENT(4);
+  else if (nv <= 8) XENT(8);
+  else if (nv <= 16) XENT(16);
+  else TORCH_CHECK(false, "xent: vocab above 65536 is not supported");
+#undef XENT
+  TORCH_CHECK(cudaGetLastError() == cudaSuccess, "softmax_xent launch failed");
+}
+
+// ---- AdamW -----------------------------------------------------------------------
+
+struct AdamParams {
+  float lr, b1, b2, eps, wd, scale_m, scale_v, grad_scale;
+};
+
+__global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+                             float* __restrict__ v, __nv_bfloat16* __restrict__ work, long n, AdamParams a) {
+  const float decay = 1.f - a.lr * a.wd;
+  for (long i = (long(blockIdx.x) * blockDim.x + threadIdx.x) * 4; i < n; i += long(gridDim.x) * blockDim.x * 4) {
+    if (i + 4 <= n) {
+      float4 pp = *reinterpret_cast<float4*>(p + i), gg = *reinterpret_cast<const float4*>(g + i);
+      float4 mm = *reinterpret_cast<float4*>(m + i), vv = *reinterpret_cast<float4*>(v + i);
+      float* P = &pp.x; float* G = &gg.x; float* M = &mm.x; float* Vv = &vv.x;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float gj = G[j] * a.grad_scale;
+        M[j] = M[j] * a.b1 + gj * (1.f - a.b1);
+        Vv[j] = Vv[j] * a.b2 + gj * gj * (1.f - a.b2);
+        const float mh = M[j] * a.scale_m, vh = Vv[j] * a.scale_v;
+        P[j] = P[j] * decay - (mh / (sqrtf(vh) + a.eps)) * a.lr;
+      }
+      *reinterpret_cast<float4*>(p + i) = pp;
+      *reinterpret_cast<float4*>(m + i) = mm;
+      *reinterpret_cast<float4*>(v + i) = vv;
+      if (work) *reinterpret_cast<uint2*>(work + i) = make_uint2(pack_bf16x2(pp.x, pp.y), pack_bf16x2(pp.z, pp.w));
+    } else {
+      for (long k = i; k < n; ++k) {
+        const float gj = g[k] * a.grad_scale;
+        m[k] = m[k] * a.b1 + gj * (1.f - a.b1);
+        v[k] = v[k] * a.b2 + gj * gj * (1.f - a.b2);
+        p[k] = p[k] * decay - ((m[k] * a.scale_m) / (sqrtf(v[k] * a.scale_v) + a.eps)) * a.lr;
+        if (work) work[k] = __float2bfloat16(p[k]);
+      }
+    }
+  }
+}
+
+void adamw_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, c10::optional<torch::Tensor> work,
+                double lr, double b1, double b2, double eps, double wd, int64_t step, double grad_scale) {
+  TORCH_CHECK(p.is_contiguous() && g.is_contiguous() && m.is_contiguous() && v.is_contiguous(), "adamw: contiguous");
+  TORCH_CHECK(p.scalar_type() == at::kFloat && g.scalar_type() == at::kFloat, "adamw: fp32");
+  const long n = p.numel();
+  TORCH_CHECK(g.numel() == n && m.numel() == n && v.numel() == n, "adamw: sizes");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(p.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(g.data_ptr()) % 16 == 0,
+              "adamw: 16-byte aligned slices");
+  __nv_bfloat16* wp = nullptr;
+  if (work.has_value()) {
+    TORCH_CHECK(work->scalar_type() == at::kBFloat16 && work->numel() == n, "adamw: work copy");
+    wp = reinterpret_cast<__nv_bfloat16*>(work->data_ptr());
+  }
+  AdamParams a;
+  a.lr = float(lr); a.b1 = float(b1); a.b2 = float(b2); a.eps = float(eps); a.wd = float(wd);
+  a.scale_m = float(1.0 / (1.0 - std::pow(b1, double(step))));
+  a.scale_v = float(1.0 / (1.0 - std::pow(b2, double(step))));
+  a.grad_scale = float(grad_scale);
+  const at::cuda::CUDAGuard guard(p.device());
+  const int threads = 256;
+  const long blocks = std::min<long>((n / 4 + threads - 1) / threads + 1, 148 * 16);
+  adamw_kernel<<<blocks, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), wp, n, a);
+  TORCH_CHECK(cudaGetLastError() == cudaSuccess, "adamw launch failed");
+}
+
+// ---- sum of squares -----------------------------------------------------------------
+
+__global__ void sumsq_kernel(const float* __restrict__ x, long n, double* out) {
+  __shared__ float red[32];
+  float s = 0.f;
+  for (long i = long(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += long(gridDim.x) * blockDim.x) s += x[i] * x[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0;
+    for (int w = 0; w < int(blockDim.x / 32); ++w) t += red[w];
+    atomicAdd(out, t);
+  }
+}
+
+// out (fp64 scalar tensor) += sum(x^2)
+void sumsq(torch::Tensor x, torch::Tensor out) {
+  TORCH_CHECK(x.scalar_type() == at::kFloat && x.is_contiguous(), "sumsq: fp32");
+  TORCH_CHECK(out.scalar_type() == at::kDouble && out.numel() == 1, "sumsq: fp64 scalar");
+  const at::cuda::CUDAGuard guard(x.device());
+  sumsq_kernel<<<148 * 4, 512, 0, at::cuda::getCurrentCUDAStream()>>>(x.data_ptr<float>(), x.numel(),
+                                                                       out.data_ptr<double>());
+  TORCH_CHECK(cudaGetLastError() == cudaSuccess, "sumsq launch failed");
+}
+
+}  // namespace nk
