@@ -7,6 +7,22 @@ namespace nk {
 void gemm(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_major, torch::Tensor C, int64_t mode,
           double alpha, c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> aux_out, int64_t splits,
           int64_t block_n);
+void rmsnorm_fwd(torch::Tensor x, torch::Tensor y, c10::optional<torch::Tensor> rstd, double eps);
+void rmsnorm_bwd(torch::Tensor x, torch::Tensor dy, torch::Tensor rstd, torch::Tensor dx, bool accum);
+void rope_qknorm_fwd(torch::Tensor qkv, torch::Tensor rstd, torch::Tensor cos_t, torch::Tensor sin_t, int64_t T,
+                     int64_t t0, int64_t H, double eps);
+void rope_qknorm_bwd(torch::Tensor qkv, torch::Tensor dqkv, torch::Tensor rstd, torch::Tensor cos_t,
+                     torch::Tensor sin_t, int64_t T, int64_t H);
+void embedding_fwd(torch::Tensor idx, torch::Tensor wte, torch::Tensor out);
+void embedding_bwd(torch::Tensor idx, torch::Tensor dx, torch::Tensor grad);
+void softmax_xent(torch::Tensor logits, torch::Tensor targets, c10::optional<torch::Tensor> nll, double grad_scale,
+                  bool write_grad);
+void adamw_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, c10::optional<torch::Tensor> work,
+                double lr, double b1, double b2, double eps, double wd, int64_t step, double grad_scale);
+void sumsq(torch::Tensor x, torch::Tensor out);
+void flash_fwd(torch::Tensor qkv, torch::Tensor out, torch::Tensor lse, int64_t B, int64_t T, int64_t H);
+void flash_bwd(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch::Tensor lse, torch::Tensor dsum,
+               torch::Tensor dqkv, int64_t B, int64_t T, int64_t H);
 }  // namespace nk
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -15,4 +31,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("B"), py::arg("b_mn_major"), py::arg("C"), py::arg("mode"), py::arg("alpha"), py::arg("aux"),
         py::arg("aux_out"), py::arg("splits"), py::arg("block_n"));
   m.def("kernel_status", &nk::kernel_status, "device error word of the kernels (0 = ok)", py::arg("reset") = true);
+  m.def("rmsnorm_fwd", &nk::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &nk::rmsnorm_bwd);
+  m.def("rope_qknorm_fwd", &nk::rope_qknorm_fwd);
+  m.def("rope_qknorm_bwd", &nk::rope_qknorm_bwd);
+  m.def("embedding_fwd", &nk::embedding_fwd);
+  m.def("embedding_bwd", &nk::embedding_bwd);
+  m.def("softmax_xent", &nk::softmax_xent);
+  m.def("adamw_step", &nk::adamw_step);
+  m.def("sumsq", &nk::sumsq);
+  m.def("flash_fwd", &nk::flash_fwd);
+  m.def("flash_bwd", &nk::flash_bwd);
 }

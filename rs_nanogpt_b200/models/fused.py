@@ -1,0 +1,180 @@
+"""Fused CUDA execution of the GPT: explicit forward and backward passes over
+the flat parameter buffers, built only from this repository's sm_100a kernels.
+
+Per block (rs-nanogpt src/model/block.rs:49-60 semantics):
+
+    h1   = rms(x)                                  rmsnorm kernel
+    qkv  = h1 Wqkv^T                               tcgen05 GEMM (one GEMM for q|k|v)
+    q,k  = rms(rope(q)), rms(rope(k))              in place, one kernel
+    y    = causal_attention(q, k, v)               flash kernel, reads qkv in place
+    x'   = x + y Wproj^T                           GEMM, residual-add epilogue
+    h2   = rms(x')
+    a,hp = relu(h2 Wfc^T)^2, h2 Wfc^T              GEMM, ReLU^2 epilogue (keeps hp)
+    x''  = x' + a Wmlp^T                           GEMM, residual-add epilogue
+
+The loss head runs chunk by chunk over the token rows: logits = rms(x_L) Wlm^T,
+then one kernel computes the fp32 log-sum-exp, the per-row NLL and, for
+training, the logits gradient in place; the lm_head data and weight gradients
+follow immediately, so the (B*T, V) logits never exist in memory at once.
+Because the loss is the last op, the lm_head backward is done during the
+forward pass.
+
+Backward mirrors the forward with dgrad GEMMs (MN-major weights), split-K
+weight-gradient GEMMs accumulating straight into the fp32 gradient buffer, the
+flash backward kernels, and RMSNorm backward kernels that add into the
+residual-stream gradient in place.
+
+Activation buffers are allocated once per batch shape and reused by every
+micro-batch.
+"""
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from ..config import GptConfig
+from ..ops import gemm
+from ..ops import layers as L
+from .params import ParamStore
+from .reference import rope_tables
+
+XENT_CHUNK_BYTES = 1 << 30  # logits bytes per loss-head chunk
+
+
+class _Workspace:
+    def __init__(self, cfg: GptConfig, batch: int, seq: int, device, train: bool):
+        m, c, nl = batch * seq, cfg.n_embd, cfg.n_layer
+        bf = dict(device=device, dtype=torch.bfloat16)
+        f32 = dict(device=device, dtype=torch.float32)
+        n_keep = nl if train else 1
+        self.x = [torch.empty(m, c, **bf) for _ in range(nl + 1)] if train else [torch.empty(m, c, **bf)] * 2
+        self.h1 = [torch.empty(m, c, **bf) for _ in range(n_keep)]
+        self.rstd1 = [torch.empty(m, **f32) for _ in range(n_keep)]
+        self.qkv = [torch.empty(m, 3 * c, **bf) for _ in range(n_keep)]
+        self.rstd_qk = [torch.empty(m * 2 * cfg.n_head, **f32) for _ in range(n_keep)]
+        self.y = [torch.empty(m, c, **bf) for _ in range(n_keep)]
+        self.lse = [torch.empty(batch * cfg.n_head * seq, **f32) for _ in range(n_keep)]
+        self.xmid = [torch.empty(m, c, **bf) for _ in range(n_keep)]
+        self.h2 = [torch.empty(m, c, **bf) for _ in range(n_keep)]
+        self.rstd2 = [torch.empty(m, **f32) for _ in range(n_keep)]
+        self.act = [torch.empty(m, 4 * c, **bf) for _ in range(n_keep)]
+        self.hpre = [torch.empty(m, 4 * c, **bf) for _ in range(n_keep)]
+        self.hf = torch.empty(m, c, **bf)
+        self.rstdf = torch.empty(m, **f32)
+        self.nll = torch.empty(m, **f32)
+        rows = max(1, min(m, XENT_CHUNK_BYTES // (2 * cfg.vocab_size)))
+        self.logits = torch.empty(rows, cfg.vocab_size, **bf)
+        if train:
+            self.dhf = torch.empty(m, c, **bf)
+            self.dx = torch.empty(m, c, **bf)
+            self.dact = torch.empty(m, 4 * c, **bf)
+            self.dh = torch.empty(m, c, **bf)
+            self.dy = torch.empty(m, c, **bf)
+            self.dqkv = torch.empty(m, 3 * c, **bf)
+            self.dsum = torch.empty(batch * cfg.n_head * seq, **f32)
+
+
+class FusedGpt:
+    def __init__(self, store: ParamStore):
+        assert store.device.type == "cuda" and store.work is not None
+        self.store = store
+        self.cfg = store.cfg
+        if self.cfg.head_dim != 128:
+            raise ValueError(f"the fused CUDA path supports head_dim 128, got {self.cfg.head_dim}")
+        cos, sin = rope_tables(self.cfg, store.device)
+        self.cos, self.sin = cos.contiguous(), sin.contiguous()
+        self._ws: Dict[Tuple[int, int, bool], _Workspace] = {}
+
+    def workspace(self, batch: int, seq: int, train: bool) -> _Workspace:
+        key = (batch, seq, train)
+        if key not in self._ws:
+            self._ws[key] = _Workspace(self.cfg, batch, seq, self.store.device, train)
+        return self._ws[key]
+
+    def _w(self, name):
+        return self.store.work_of(name)
+
+    def _forward_blocks(self, idx: torch.Tensor, ws: _Workspace, train: bool) -> torch.Tensor:
+        cfg, st = self.cfg, self.store
+        b, t = idx.shape
+        eps = cfg.norm_eps
+        x = L.embedding(idx, st.param("wte.weight"), out=ws.x[0])
+        for i in range(cfg.n_layer):
+            j = i if train else 0
+            p = f"blocks.{i}."
+            h1 = L.rmsnorm(x, eps, out=ws.h1[j], rstd=ws.rstd1[j])
+            qkv = gemm.linear(h1, st.qkv_work(i), out=ws.qkv[j])
+            L.rope_qknorm(qkv, ws.rstd_qk[j], self.cos, self.sin, t, cfg.n_head, eps)
+            L.flash_attention(qkv, ws.y[j], ws.lse[j], b, t, cfg.n_head)
+            xmid = gemm.linear_residual(ws.y[j], self._w(p + "attn.c_proj.weight"), x, out=ws.xmid[j])
+            h2 = L.rmsnorm(xmid, eps, out=ws.h2[j], rstd=ws.rstd2[j])
+            gemm.linear_relu2(h2, self._w(p + "mlp.c_fc.weight"), act=ws.act[j], h=ws.hpre[j])
+            x_next = ws.x[i + 1] if train else ws.x[(i + 1) % 2]
+            x = gemm.linear_residual(ws.act[j], self._w(p + "mlp.c_proj.weight"), xmid, out=x_next)
+        return L.rmsnorm(x, eps, out=ws.hf, rstd=ws.rstdf)
+
+    def _loss_head(self, hf: torch.Tensor, targets: torch.Tensor, ws: _Workspace, grad_scale: Optional[float]):
+        """Chunked lm_head + cross-entropy. With grad_scale set, also computes
+        d(hf) into ws.dhf and accumulates the lm_head weight gradient."""
+        st = self.store
+        w = self._w("lm_head.weight")
+        m = hf.shape[0]
+        rows = ws.logits.shape[0]
+        tg = targets.reshape(-1)
+        for r0 in range(0, m, rows):
+            r1 = min(m, r0 + rows)
+            logits = ws.logits[: r1 - r0]
+            gemm.linear(hf[r0:r1], w, out=logits)
+            train = grad_scale is not None
+            L.softmax_xent(logits, tg[r0:r1], ws.nll[r0:r1], grad_scale or 0.0, train)
+            if train:
+                gemm.linear_dgrad(logits, w, out=ws.dhf[r0:r1])
+                gemm.linear_wgrad(logits, hf[r0:r1], st.grad_of("lm_head.weight"))
+        return ws.nll
+
+    @torch.no_grad()
+    def forward_loss(self, idx: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        """Per-position NLL (B*T,) fp32 without gradients (eval)."""
+        b, t = idx.shape
+        ws = self.workspace(b, t, False)
+        hf = self._forward_blocks(idx, ws, train=False)
+        return self._loss_head(hf, targets, ws, None)
+
+    @torch.no_grad()
+    def forward_logits(self, idx: torch.Tensor) -> torch.Tensor:
+        b, t = idx.shape
+        ws = self.workspace(b, t, False)
+        hf = self._forward_blocks(idx, ws, train=False)
+        return gemm.linear(hf, self._w("lm_head.weight")).view(b, t, -1)
+
+    @torch.no_grad()
+    def forward_backward(self, idx: torch.Tensor, targets: torch.Tensor, loss_scale: float):
+        """One micro-batch. Gradients of ``loss_scale * sum(nll)`` are added to
+        the store's fp32 gradient buffer. Returns the per-position NLL and
+        the validity mask (device tensors)."""
+        cfg, st = self.cfg, self.store
+        b, t = idx.shape
+        eps = cfg.norm_eps
+        ws = self.workspace(b, t, True)
+        hf = self._forward_blocks(idx, ws, train=True)
+        nll = self._loss_head(hf, targets, ws, loss_scale)
+        # Final norm backward: dx = d rms(x_L).
+        dx = L.rmsnorm_bwd(ws.x[cfg.n_layer], ws.dhf, ws.rstdf, dx=ws.dx, accumulate=False)
+        for i in reversed(range(cfg.n_layer)):
+            p = f"blocks.{i}."
+            w_mlp, w_fc = self._w(p + "mlp.c_proj.weight"), self._w(p + "mlp.c_fc.weight")
+            # MLP: x'' = x' + relu(h2 Wfc^T)^2 Wmlp^T
+            gemm.linear_wgrad(dx, ws.act[i], st.grad_of(p + "mlp.c_proj.weight"))
+            gemm.linear_dgrad_drelu2(dx, w_mlp, ws.hpre[i], out=ws.dact)
+            gemm.linear_wgrad(ws.dact, ws.h2[i], st.grad_of(p + "mlp.c_fc.weight"))
+            gemm.linear_dgrad(ws.dact, w_fc, out=ws.dh)
+            L.rmsnorm_bwd(ws.xmid[i], ws.dh, ws.rstd2[i], dx=dx, accumulate=True)
+            # Attention: x' = x + attn(rms(x)) Wproj^T
+            gemm.linear_wgrad(dx, ws.y[i], st.grad_of(p + "attn.c_proj.weight"))
+            gemm.linear_dgrad(dx, self._w(p + "attn.c_proj.weight"), out=ws.dy)
+            L.flash_attention_bwd(ws.qkv[i], ws.y[i], ws.dy, ws.lse[i], ws.dsum, ws.dqkv, b, t, cfg.n_head)
+            L.rope_qknorm_bwd(ws.qkv[i], ws.dqkv, ws.rstd_qk[i], self.cos, self.sin, t, cfg.n_head)
+            gemm.linear_wgrad(ws.dqkv, ws.h1[i], st.qkv_grad(i))
+            gemm.linear_dgrad(ws.dqkv, st.qkv_work(i), out=ws.dh)
+            L.rmsnorm_bwd(ws.x[i], ws.dh, ws.rstd1[i], dx=dx, accumulate=True)
+        L.embedding_bwd(idx, dx, st.grad_of("wte.weight"))
+        return nll

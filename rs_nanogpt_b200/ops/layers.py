@@ -1,0 +1,68 @@
+"""Thin Python wrappers of the non-GEMM sm_100a kernels.
+
+Kernels: ``csrc/kernels/norm_rope.cu`` (RMSNorm, RoPE + QK-norm),
+``csrc/kernels/embed_loss_optim.cu`` (embedding, softmax cross-entropy, AdamW,
+sum of squares) and ``csrc/kernels/flash_attn.cu`` (causal flash attention).
+"""
+from typing import Optional
+
+import torch
+
+from ._ext import ext
+
+
+def rmsnorm(x: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None,
+            rstd: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty_like(x)
+    ext().rmsnorm_fwd(x, out, rstd, eps)
+    return out
+
+
+def rmsnorm_bwd(x, dy, rstd, dx: Optional[torch.Tensor] = None, accumulate: bool = False) -> torch.Tensor:
+    if dx is None:
+        dx = torch.empty_like(x)
+        accumulate = False
+    ext().rmsnorm_bwd(x, dy, rstd, dx, accumulate)
+    return dx
+
+
+def rope_qknorm(qkv, rstd, cos, sin, seq_len: int, n_head: int, eps: float, t0: int = 0) -> None:
+    """In place on the q and k column blocks of ``qkv`` (tokens, 3C)."""
+    ext().rope_qknorm_fwd(qkv, rstd, cos, sin, seq_len, t0, n_head, eps)
+
+
+def rope_qknorm_bwd(qkv, dqkv, rstd, cos, sin, seq_len: int, n_head: int) -> None:
+    ext().rope_qknorm_bwd(qkv, dqkv, rstd, cos, sin, seq_len, n_head)
+
+
+def embedding(idx: torch.Tensor, wte: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(idx.numel(), wte.shape[1], device=wte.device, dtype=torch.bfloat16)
+    ext().embedding_fwd(idx.reshape(-1), wte, out)
+    return out
+
+
+def embedding_bwd(idx: torch.Tensor, dx: torch.Tensor, grad: torch.Tensor) -> None:
+    ext().embedding_bwd(idx.reshape(-1), dx, grad)
+
+
+def softmax_xent(logits, targets, nll: Optional[torch.Tensor] = None, grad_scale: float = 0.0,
+                 write_grad: bool = False) -> None:
+    ext().softmax_xent(logits, targets, nll, grad_scale, write_grad)
+
+
+def adamw(p, g, m, v, work, lr, b1, b2, eps, wd, step, grad_scale=1.0) -> None:
+    ext().adamw_step(p, g, m, v, work, lr, b1, b2, eps, wd, step, grad_scale)
+
+
+def sumsq(x: torch.Tensor, out: torch.Tensor) -> None:
+    ext().sumsq(x, out)
+
+
+def flash_attention(qkv, out, lse, batch: int, seq_len: int, n_head: int) -> None:
+    ext().flash_fwd(qkv, out, lse, batch, seq_len, n_head)
+
+
+def flash_attention_bwd(qkv, out, dout, lse, dsum, dqkv, batch: int, seq_len: int, n_head: int) -> None:
+    ext().flash_bwd(qkv, out, dout, lse, dsum, dqkv, batch, seq_len, n_head)
