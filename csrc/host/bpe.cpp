@@ -4,9 +4,7 @@
 #include <atomic>
 #include <cstdio>
 #include <cstdlib>
-#include <fstream>
 #include <queue>
-#include <sstream>
 #include <stdexcept>
 #include <thread>
 #include <tuple>
@@ -71,19 +69,18 @@ std::string base64_decode(std::string_view in) {
 }
 
 static std::string debug_bytes(const std::string& b) {
-  std::ostringstream os;
-  os << "[";
-  for (size_t i = 0; i < b.size(); ++i) os << (i ? ", " : "") << unsigned(uint8_t(b[i]));
-  os << "]";
-  return os.str();
+  std::string s = "[";
+  for (size_t i = 0; i < b.size(); ++i) s += (i ? ", " : "") + std::to_string(unsigned(uint8_t(b[i])));
+  return s + "]";
 }
 
 Tokenizer Tokenizer::from_file(const std::string& path) {
-  std::ifstream f(path, std::ios::binary);
+  FILE* f = std::fopen(path.c_str(), "rb");
   if (!f) throw std::runtime_error("cannot open vocab file " + path);
-  std::stringstream ss;
-  ss << f.rdbuf();
-  std::string contents = ss.str();
+  std::string contents;
+  char buf[1 << 16];
+  for (size_t n; (n = std::fread(buf, 1, sizeof buf, f)) > 0;) contents.append(buf, n);
+  std::fclose(f);
 
   std::vector<std::pair<uint32_t, std::string>> entries;
   size_t pos = 0, line_no = 0;

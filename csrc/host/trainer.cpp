@@ -3,7 +3,6 @@
 #include <algorithm>
 #include <atomic>
 #include <cstdio>
-#include <fstream>
 #include <queue>
 #include <stdexcept>
 #include <string_view>
@@ -187,12 +186,17 @@ std::vector<std::string> BpeTrainer::train(size_t num_merges, int progress) {
 }
 
 void write_vocab(const std::string& path, const std::vector<std::string>& merges) {
-  std::ofstream f(path, std::ios::binary | std::ios::trunc);
-  if (!f) throw std::runtime_error("cannot write vocab file " + path);
+  // C stdio rather than iostreams: the module shares a process with other
+  // native libraries (Arrow) whose C++ runtime state iostreams would touch.
+  std::string text;
   size_t rank = 0;
-  for (int i = 0; i < 256; ++i) f << base64_encode(std::string(1, char(i))) << ' ' << rank++ << '\n';
-  for (const auto& m : merges) f << base64_encode(m) << ' ' << rank++ << '\n';
-  if (!f) throw std::runtime_error("failed writing vocab file " + path);
+  for (int i = 0; i < 256; ++i) text += base64_encode(std::string(1, char(i))) + ' ' + std::to_string(rank++) + '\n';
+  for (const auto& m : merges) text += base64_encode(m) + ' ' + std::to_string(rank++) + '\n';
+  FILE* f = std::fopen(path.c_str(), "wb");
+  if (!f) throw std::runtime_error("cannot write vocab file " + path);
+  const size_t n = std::fwrite(text.data(), 1, text.size(), f);
+  const int rc = std::fclose(f);
+  if (n != text.size() || rc != 0) throw std::runtime_error("failed writing vocab file " + path);
 }
 
 }  // namespace nanogpt_host

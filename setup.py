@@ -20,7 +20,7 @@ def host_extension():
     srcs = sorted(glob.glob(os.path.join("csrc", "host", "*.cpp")))
     return Pybind11Extension(
         "rs_nanogpt_b200._host", srcs, cxx_std=17,
-        extra_compile_args=["-O3", "-pthread", "-fvisibility=hidden"], extra_link_args=["-pthread"])
+        extra_compile_args=["-O3", "-pthread", "-fvisibility=hidden"], extra_link_args=["-pthread", "-static-libstdc++", "-static-libgcc"])
 
 
 def cuda_extension():
