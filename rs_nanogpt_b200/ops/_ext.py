@@ -3,8 +3,31 @@
 The extension is built in-tree (``python setup.py build_ext --inplace``).
 On a machine with a GPU the kernels are the only implementation of the hot
 ops, so a missing extension is an error, never a silent fallback.
+
+Every call into the extension goes through a counting proxy, so callers such
+as ``bench.py`` can report how many of this package's kernels were launched
+(``launch_count``).
 """
 import functools
+
+# Kernels launched per extension call (1 unless listed).
+_LAUNCHES = {"flash_bwd": 3, "kernel_status": 0}
+_count = [0]
+
+
+class _Counted:
+    def __init__(self, mod):
+        self._mod = mod
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        n = _LAUNCHES.get(name, 1)
+
+        def call(*args, **kwargs):
+            _count[0] += n
+            return fn(*args, **kwargs)
+
+        return call
 
 
 @functools.lru_cache(maxsize=None)
@@ -14,7 +37,11 @@ def ext():
     except ImportError as e:
         raise RuntimeError(
             "rs_nanogpt_b200._C is not built; run `python setup.py build_ext --inplace`") from e
-    return _C
+    return _Counted(_C)
+
+
+def launch_count() -> int:
+    return _count[0]
 
 
 def kernel_status(reset: bool = True) -> int:

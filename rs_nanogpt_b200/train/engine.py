@@ -1,0 +1,115 @@
+"""The training step as a library call.
+
+``TrainEngine`` owns the flat parameters, the model executor (the fused CUDA
+engine on a GPU, the PyTorch reference on CPU), the grouped AdamW and the
+data-parallel context. ``step(batches)`` runs one optimizer step over
+``grad_accum`` micro-batches with the reference's loss scaling
+(rs-nanogpt src/train/train_loop.rs:200-293, :435-524):
+
+* each micro-batch backprops ``sum(nll) / tokens_per_step`` (per-rank expected
+  tokens); the cross-rank gradient mean supplies the remaining 1/world;
+* with ignorable targets (SFT) the gradient is then rescaled by
+  ``expected * world / global_valid_count`` -- folded into the optimizer
+  kernel's gradient scale instead of a separate pass over the gradients;
+* gradients are averaged across ranks, then AdamW runs with the scheduled LR.
+"""
+from dataclasses import dataclass
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+
+from ..models.params import ParamStore
+from ..parallel.dist import DistCtx
+from .optim import GroupedAdamW, GroupLrs, GroupWeightDecay
+
+
+@dataclass
+class StepStats:
+    nll_sum: torch.Tensor     # device scalar, fp32 (sum over this rank's tokens)
+    valid_count: torch.Tensor  # device scalar, fp32
+
+
+class TrainEngine:
+    def __init__(self, store: ParamStore, lrs: GroupLrs, wd: GroupWeightDecay = GroupWeightDecay(),
+                 dist: Optional[DistCtx] = None, comm: str = "nccl"):
+        self.store = store
+        self.cfg = store.cfg
+        self.dist = dist or DistCtx.single(store.device)
+        self.opt = GroupedAdamW(store, lrs, self.cfg.n_embd, wd)
+        self.comm = comm
+        self.fused_ddp = None
+        if store.device.type == "cuda":
+            from ..models.fused import FusedGpt
+            self.model = FusedGpt(store)
+        else:
+            from ..models.reference import ReferenceGpt
+            self.model = ReferenceGpt(store, torch.float32)
+        if comm == "fused" and self.dist.world_size() > 1:
+            from ..parallel.fused_ddp import FusedDdp
+            self.fused_ddp = FusedDdp(store, self.opt, self.dist)
+
+    # -- pieces ---------------------------------------------------------------------
+    def micro_backward(self, inputs: torch.Tensor, targets: torch.Tensor, loss_scale: float) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Adds d(loss_scale * sum nll)/dtheta to the gradient buffer; returns
+        (sum nll, valid count) as device scalars."""
+        if self.store.device.type == "cuda":
+            nll = self.model.forward_backward(inputs, targets, loss_scale)
+            valid = (targets.reshape(-1) >= 0).sum(dtype=torch.float32)
+            return nll.sum(), valid
+        from ..models.reference import cross_entropy_sum_count
+        st = self.store
+        st.master.requires_grad_(True)
+        try:
+            s, cnt = cross_entropy_sum_count(self.model.forward(inputs), targets)
+            (s * loss_scale).backward()
+            st.grad.add_(st.master.grad)
+        finally:
+            st.master.grad = None
+            st.master.requires_grad_(False)
+        return s.detach(), cnt
+
+    def step(self, batches: Sequence[Tuple[torch.Tensor, torch.Tensor]], tokens_per_step: int, lr_mult: float,
+             targets_may_be_ignored: bool = False) -> StepStats:
+        st = self.store
+        st.zero_grad()
+        inv = 1.0 / tokens_per_step
+        nll_sum = torch.zeros((), dtype=torch.float32, device=st.device)
+        count = torch.zeros((), dtype=torch.float32, device=st.device)
+        for inputs, targets in batches:
+            b, t = inputs.shape
+            assert len(batches) * b * t == tokens_per_step, (
+                f"batch shape ({b}, {t}) x grad_accum disagrees with tokens_per_step {tokens_per_step}")
+            s, c = self.micro_backward(inputs, targets, inv)
+            nll_sum += s
+            count += c
+        grad_scale = 1.0
+        if targets_may_be_ignored:
+            # expected * world / global count (== 1 when nothing is ignored).
+            global_count = self.dist.all_reduce_sum_tensor(count.clone())
+            grad_scale = float(tokens_per_step * self.dist.world_size()) / max(float(global_count.item()), 1.0)
+            if float(global_count.item()) == 0.0:
+                grad_scale = 0.0
+        self.opt.set_lr_mult(lr_mult)
+        if self.fused_ddp is not None:
+            self.fused_ddp.reduce_and_step(grad_scale)
+        else:
+            self.dist.all_reduce_grads(st.grad)
+            self.opt.step(grad_scale)
+        return StepStats(nll_sum, count)
+
+    def grad_norm(self) -> float:
+        st = self.store
+        if st.device.type == "cuda":
+            from ..ops import layers as L
+            out = torch.zeros(1, dtype=torch.float64, device=st.device)
+            L.sumsq(st.grad, out)
+            return float(out.item()) ** 0.5
+        return float(st.grad.double().pow(2).sum().item()) ** 0.5
+
+    @torch.no_grad()
+    def eval_nll(self, inputs: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        """Per-position NLL (B, T), 0 where ignored."""
+        if self.store.device.type == "cuda":
+            return self.model.forward_loss(inputs, targets).view(targets.shape).clone()
+        from ..models.reference import cross_entropy_none
+        return cross_entropy_none(self.model.forward(inputs), targets)
