@@ -3,7 +3,8 @@
 //
 //   warp 0      TMA producer: 128B-swizzled A/B tiles into a STAGES-deep ring
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2..5  epilogue: tcgen05.ld from TMEM, fused elementwise op, store
+//   warps 2..9  epilogue: tcgen05.ld from TMEM, fused elementwise op, store
+//               (two warps per TMEM lane quarter, each owning half the columns)
 //
 // The fp32 accumulator of a 128 x BN tile lives in tensor memory; two
 // accumulator buffers let the epilogue of tile i overlap the MMAs of tile i+1.
@@ -49,6 +50,7 @@ struct GemmArgs {
 };
 
 constexpr int BM = 128, BK = 64, kGroupM = 16;
+constexpr int kEpiWarps = 8, kThreads = 64 + 32 * kEpiWarps;
 
 template <int BN>
 struct Smem {
@@ -150,7 +152,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int row, int c
 }
 
 template <int BN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const GemmArgs args) {
   using S = Smem<BN>;
@@ -168,7 +170,7 @@ __global__ void __launch_bounds__(192, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
-    for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], 4); }
+    for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], kEpiWarps); }
     fence_barrier_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
@@ -243,7 +245,8 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int q = warp & 3;                 // TMEM lane quarter this warp may access
+    const int half = (warp - 2) / 4;        // which half of the tile's columns
     int local = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
       int m, n, kb0, kb1;
@@ -254,7 +257,7 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const int row = m * BM + q * 32 + lane;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
         float v[32];
         tmem_ld_32x32(tmem_base + (uint32_t(q * 32) << 16) + b * BN + c * 32, v);
         const int col0 = n * BN + c * 32;
@@ -294,7 +297,7 @@ static void launch(const GemmArgs& args, const CUtensorMap& ta, const CUtensorMa
   }
   const int units = args.num_m * args.num_n * args.splits;
   const int grid = std::min(units, num_sms());
-  gemm_bf16_kernel<BN><<<grid, 192, Smem<BN>::kTotal, stream>>>(ta, tb, args);
+  gemm_bf16_kernel<BN><<<grid, kThreads, Smem<BN>::kTotal, stream>>>(ta, tb, args);
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "gemm launch failed");
 }
 
