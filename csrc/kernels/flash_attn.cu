@@ -552,3 +552,110 @@ void flash_bwd(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch::
 }
 
 }  // namespace nk
+
+// ---------------------------------------------------------------------------------------------
+// Allocation-free C entry point (declared and documented in noalloc.h): the same
+// three backward kernels, with the D = rowsum(dO o O) scratch taken from a fixed
+// file-scope device array instead of a caller-provided tensor.
+#include <mutex>
+
+#include "noalloc.h"
+
+static __device__ __align__(256) float g_noalloc_dsum[NANOGPT_NOALLOC_MAX_ROWS];
+
+namespace {
+constexpr int kNoallocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kNoallocMaxDevices] = {};
+
+bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) const char* nanogpt_noalloc_error_string(int code) {
+  switch (code) {
+    case NANOGPT_NOALLOC_OK: return "ok";
+    case NANOGPT_NOALLOC_ERR_TOO_LARGE:
+      return "batch * n_head * seq_len exceeds the fixed scratch of NANOGPT_NOALLOC_MAX_ROWS (1048576) floats";
+    case NANOGPT_NOALLOC_ERR_BAD_ARG:
+      return "invalid argument (null or unaligned pointer, head_dim not 64/128, or non-positive size)";
+    case NANOGPT_NOALLOC_ERR_CUDA: return "a CUDA runtime call failed (see cudaGetLastError)";
+    default: return "unknown error code";
+  }
+}
+
+extern "C" __attribute__((visibility("default"))) int nanogpt_flash_attention_bwd_noalloc(
+    const void* qkv, const void* out, const void* dout, const float* lse, void* dqkv, int batch, int seq_len,
+    int n_head, int head_dim, cudaStream_t stream) {
+  using namespace nk;
+  if (!qkv || !out || !dout || !lse || !dqkv) return NANOGPT_NOALLOC_ERR_BAD_ARG;
+  if (!aligned16(qkv) || !aligned16(out) || !aligned16(dout) || !aligned16(dqkv)) return NANOGPT_NOALLOC_ERR_BAD_ARG;
+  if (batch <= 0 || seq_len <= 0 || n_head <= 0 || (head_dim != 64 && head_dim != 128))
+    return NANOGPT_NOALLOC_ERR_BAD_ARG;
+  const size_t rows = size_t(batch) * size_t(n_head) * size_t(seq_len);
+  if (rows > NANOGPT_NOALLOC_MAX_ROWS) return NANOGPT_NOALLOC_ERR_TOO_LARGE;
+
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return NANOGPT_NOALLOC_ERR_CUDA;
+  if (dev < 0 || dev >= kNoallocMaxDevices) return NANOGPT_NOALLOC_ERR_BAD_ARG;
+  float* scratch = nullptr;
+  {
+    // One-time set-up per device, with that device current: the host-side
+    // symbol is only a stand-in, the kernels need the device address.
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_noalloc_dsum) != cudaSuccess || !p) return NANOGPT_NOALLOC_ERR_CUDA;
+      g_noalloc_ptr[dev] = static_cast<float*>(p);
+    }
+    scratch = g_noalloc_ptr[dev];
+  }
+
+  const long C = long(n_head) * head_dim;
+  AttnArgs a{};
+  auto base = static_cast<const __nv_bfloat16*>(qkv);
+  a.q = base; a.k = base + C; a.v = base + 2 * C;
+  a.ld_qkv = 3 * C;
+  a.B = batch; a.H = n_head; a.T = seq_len;
+  a.scale = 1.f / std::sqrt(float(head_dim));
+  a.sl2 = a.scale * kLog2e;
+  a.o = static_cast<const __nv_bfloat16*>(out);
+  a.dout = static_cast<const __nv_bfloat16*>(dout);
+  a.ld_do = C;
+  a.lse = const_cast<float*>(lse);
+  a.dsum = scratch;
+
+  AttnArgs d = a;
+  d.ld_out = C;
+  auto dbase = static_cast<__nv_bfloat16*>(dqkv);
+  AttnArgs q = a;
+  q.out = dbase;
+  q.ld_out = 3 * C;
+  AttnArgs kv = a;
+  kv.out = dbase + C;
+  kv.out2 = dbase + 2 * C;
+  kv.ld_out = 3 * C;
+  const long items = long(batch) * seq_len * n_head;
+  dim3 gq(unsigned((seq_len + 127) / 128), unsigned(batch * n_head));
+  dim3 gk(unsigned((seq_len + 63) / 64), unsigned(batch * n_head));
+  cudaError_t e = cudaSuccess;
+  if (head_dim == 128) {
+    const int smq = (2 * 128 + 4 * 64) * 128 * 2, smk = (2 * 64 + 4 * 32) * 128 * 2 + 4 * 32 * 4;
+    e = cudaFuncSetAttribute(flash_bwd_dq_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smq);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(flash_bwd_dkv_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smk);
+    if (e != cudaSuccess) return NANOGPT_NOALLOC_ERR_CUDA;
+    flash_bwd_dot_kernel<128><<<unsigned((items + 7) / 8), 256, 0, stream>>>(d);
+    flash_bwd_dq_kernel<128><<<gq, 256, smq, stream>>>(q);
+    flash_bwd_dkv_kernel<128><<<gk, 128, smk, stream>>>(kv);
+  } else {
+    const int smq = (2 * 128 + 4 * 64) * 64 * 2, smk = (2 * 64 + 4 * 32) * 64 * 2 + 4 * 32 * 4;
+    e = cudaFuncSetAttribute(flash_bwd_dq_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smq);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(flash_bwd_dkv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smk);
+    if (e != cudaSuccess) return NANOGPT_NOALLOC_ERR_CUDA;
+    flash_bwd_dot_kernel<64><<<unsigned((items + 7) / 8), 256, 0, stream>>>(d);
+    flash_bwd_dq_kernel<64><<<gq, 256, smq, stream>>>(q);
+    flash_bwd_dkv_kernel<64><<<gk, 128, smk, stream>>>(kv);
+  }
+  return cudaGetLastError() == cudaSuccess ? NANOGPT_NOALLOC_OK : NANOGPT_NOALLOC_ERR_CUDA;
+}
