@@ -96,8 +96,8 @@ def parse_meta(contents: str) -> CheckpointMeta:
         if k not in vals:
             raise CheckpointError(f"checkpoint meta: missing key `{k}`")
     cfg = GptConfig(vocab_size=vals["vocab_size"], sequence_len=vals["sequence_len"], n_layer=vals["n_layer"],
-                    n_head=vals["n_head"], n_embd=vals["n_embd"], rope_base=float(np.float32(vals["rope_base"])),
-                    norm_eps=float(np.float32(vals["norm_eps"])))
+                    n_head=vals["n_head"], n_embd=vals["n_embd"], rope_base=float(vals["rope_base"]),
+                    norm_eps=float(vals["norm_eps"]))
     return CheckpointMeta(cfg, vals["step"], float(vals["val_bpb"]))
 
 
