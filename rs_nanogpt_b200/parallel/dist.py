@@ -150,8 +150,16 @@ class DistCtx:
             return torch.device(self.device)
         return torch.device("cpu")
 
-    def shutdown(self) -> None:
-        if self._world > 1:
+    def shutdown(self, clean: bool = True) -> None:
+        """Leave the process group. After a failure (clean=False) nothing is
+        collective: this rank just exits and the launcher's supervisor stops
+        the others, exactly as when a rank dies."""
+        if self._world > 1 and clean:
             import torch.distributed as dist
             if dist.is_initialized():
-                dist.destroy_process_group()
+                # All ranks leave together: tearing down a connection while a
+                # peer still uses it aborts that peer's transport thread.
+                try:
+                    self.barrier()
+                finally:
+                    dist.destroy_process_group()

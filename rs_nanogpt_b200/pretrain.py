@@ -43,6 +43,7 @@ def print_config_summary(c: GptConfig) -> None:
 def run_pretrain(args, env) -> None:
     device = select_device(args.device, env)
     dist = init_dist(env, device)
+    ok = False
     try:
         accum = validate_batch_geometry(args.gpus, args.device_batch, args.sequence_len, args.total_batch)
         tok = BpeTokenizer.from_file(args.vocab)
@@ -95,8 +96,9 @@ def run_pretrain(args, env) -> None:
         train(engine, loader, tcfg, ev, fault=_fault_from_env(dist))
         loader.close()
         metrics.close()
+        ok = True
     finally:
-        dist.shutdown()
+        dist.shutdown(clean=ok)
 
 
 def _fault_from_env(dist):

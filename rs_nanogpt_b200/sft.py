@@ -166,6 +166,7 @@ def run_sft(args, env) -> None:
     device = select_device(args.device, env)
     dist = init_dist(env, device)
     run_dir = None
+    ok = False
     try:
         if args.gpus != dist.world_size():
             raise SftError(f"--gpus {args.gpus} disagrees with the distributed world size {dist.world_size()}")
@@ -243,8 +244,9 @@ def run_sft(args, env) -> None:
                          save_optimizer=args.save_optimizer)
         train(engine, view, tcfg, ev)
         metrics.close()
+        ok = True
     finally:
         # A run that failed before writing anything leaves no empty run dir behind.
         if run_dir is not None and os.path.isdir(run_dir) and not os.listdir(run_dir):
             os.rmdir(run_dir)
-        dist.shutdown()
+        dist.shutdown(clean=ok)
