@@ -3,8 +3,9 @@
 //
 //   warp 0      TMA producer: 128B-swizzled A/B tiles into a STAGES-deep ring
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2..9  epilogue: tcgen05.ld from TMEM, fused elementwise op, store
-//               (two warps per TMEM lane quarter, each owning half the columns)
+//   warps 2..9  epilogue: tcgen05.ld from TMEM, fused elementwise op, staged in
+//               shared memory and written with TMA tensor stores (two warps per
+//               TMEM lane quarter, each owning half the columns)
 //
 // The fp32 accumulator of a 128 x BN tile lives in tensor memory; two
 // accumulator buffers let the epilogue of tile i overlap the MMAs of tile i+1.
@@ -58,7 +59,8 @@ struct Smem {
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kTotal = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kTotal = kStages * kStageBytes + kEpiWarps * 2 * 2048 /*epilogue staging*/ +
+                                1024 /*align*/ + 512 /*barriers*/;
 };
 
 // Work unit -> (tile row m, tile col n, k-block range). Tiles are rastered in
@@ -77,93 +79,66 @@ __device__ __forceinline__ void unit_coords(const GemmArgs& a, int u, int& m, in
   kb1 = min(a.kb_total, kb0 + a.kb_per_split);
 }
 
-__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* p, const float (&x)[32]) {
-  uint4* q = reinterpret_cast<uint4*>(p);
+// Epilogue staging: each epilogue warp owns two 2 KB shared-memory buffers
+// holding a 32-row x 32-column bf16 chunk in the TMA 64-byte swizzle layout
+// (16-byte chunk j of row r sits at chunk j ^ ((r >> 1) & 3)). Outputs leave
+// through TMA tensor stores and the residual / pre-activation input arrives
+// through TMA tensor loads, so no thread issues row-scattered global accesses.
+constexpr int kStageBufBytes = 2048;
+
+__device__ __forceinline__ uint32_t stg_off(int r, int j) { return uint32_t(r * 64 + ((j ^ ((r >> 1) & 3)) << 4)); }
+
+__device__ __forceinline__ void stage_row_store(uint8_t* buf, int r, const float (&x)[32]) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
-    q[i] = make_uint4(pack_bf16x2(x[8 * i], x[8 * i + 1]), pack_bf16x2(x[8 * i + 2], x[8 * i + 3]),
-                      pack_bf16x2(x[8 * i + 4], x[8 * i + 5]), pack_bf16x2(x[8 * i + 6], x[8 * i + 7]));
+  for (int j = 0; j < 4; ++j)
+    *reinterpret_cast<uint4*>(buf + stg_off(r, j)) =
+        make_uint4(pack_bf16x2(x[8 * j], x[8 * j + 1]), pack_bf16x2(x[8 * j + 2], x[8 * j + 3]),
+                   pack_bf16x2(x[8 * j + 4], x[8 * j + 5]), pack_bf16x2(x[8 * j + 6], x[8 * j + 7]));
 }
 
-__device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int row, int col0, const float (&v)[32]) {
+__device__ __forceinline__ void stage_row_load(const uint8_t* buf, int r, float (&y)[32]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 w = *reinterpret_cast<const uint4*>(buf + stg_off(r, j));
+    uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float2 f = unpack_bf16x2(ws[k]);
+      y[8 * j + 2 * k] = f.x;
+      y[8 * j + 2 * k + 1] = f.y;
+    }
+  }
+}
+
+__device__ __forceinline__ void atomic_chunk(const GemmArgs& a, int row, int col0, const float (&v)[32]) {
   if (row >= a.M) return;
-  const bool full = col0 + 32 <= a.N;
-  if (a.mode == kAtomicF32) {
-    float* c = reinterpret_cast<float*>(a.C) + long(row) * a.ldc + col0;
-    if (full) {
+  float* c = reinterpret_cast<float*>(a.C) + long(row) * a.ldc + col0;
+  if (col0 + 32 <= a.N) {
 #pragma unroll
-      for (int i = 0; i < 32; i += 4)
-        atomicAdd(reinterpret_cast<float4*>(c + i), make_float4(a.alpha * v[i], a.alpha * v[i + 1],
-                                                                a.alpha * v[i + 2], a.alpha * v[i + 3]));
-    } else {
-      for (int i = 0; i < 32 && col0 + i < a.N; ++i) atomicAdd(c + i, a.alpha * v[i]);
-    }
-    return;
+    for (int i = 0; i < 32; i += 4)
+      atomicAdd(reinterpret_cast<float4*>(c + i),
+                make_float4(a.alpha * v[i], a.alpha * v[i + 1], a.alpha * v[i + 2], a.alpha * v[i + 3]));
+  } else {
+    for (int i = 0; i < 32 && col0 + i < a.N; ++i) atomicAdd(c + i, a.alpha * v[i]);
   }
-  __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(a.C) + long(row) * a.ldc + col0;
-  float x[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) x[i] = a.alpha * v[i];
-  if (a.mode == kRelu2) {
-    __nv_bfloat16* h = a.aux_out + long(row) * a.ld_aux_out + col0;
-    if (full) store_bf16x32(h, x);
-    else
-      for (int i = 0; i < 32 && col0 + i < a.N; ++i) h[i] = __float2bfloat16(x[i]);
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      // Square the bf16-rounded pre-activation, as relu(h)^2 on a bf16 h would.
-      float hr = fmaxf(__bfloat162float(__float2bfloat16(x[i])), 0.f);
-      x[i] = hr * hr;
-    }
-  } else if (a.mode == kDRelu2 || a.mode == kResidual) {
-    const __nv_bfloat16* s = a.aux + long(row) * a.ld_aux + col0;
-    float y[32];
-    if (full) {
-      const uint4* sp = reinterpret_cast<const uint4*>(s);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        uint4 w = sp[i];
-        uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float2 f = unpack_bf16x2(ws[j]);
-          y[8 * i + 2 * j] = f.x;
-          y[8 * i + 2 * j + 1] = f.y;
-        }
-      }
-    } else {
-      for (int i = 0; i < 32; ++i) y[i] = col0 + i < a.N ? __bfloat162float(s[i]) : 0.f;
-    }
-    if (a.mode == kDRelu2) {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        // d/dh relu(h)^2 = 2 relu(h), applied to the bf16-rounded upstream grad.
-        float g = __bfloat162float(__float2bfloat16(x[i]));
-        x[i] = g * 2.f * fmaxf(y[i], 0.f);
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) x[i] = __bfloat162float(__float2bfloat16(x[i])) + y[i];
-    }
-  }
-  if (full) store_bf16x32(c, x);
-  else
-    for (int i = 0; i < 32 && col0 + i < a.N; ++i) c[i] = __float2bfloat16(x[i]);
 }
 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX,
                      const GemmArgs args) {
   using S = Smem<BN>;
   constexpr int STAGES = S::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * S::kStageBytes);
+  uint8_t* staging = smem + STAGES * S::kStageBytes;  // kEpiWarps x 2 x 2 KB, 1024-aligned
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(staging + kEpiWarps * 2 * kStageBufBytes);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* acc_full = empty_bar + STAGES;
   uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* aux_bar = acc_empty + 2;  // one per epilogue warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bar + kEpiWarps);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int units = args.num_m * args.num_n * args.splits;
@@ -171,6 +146,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
     for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], kEpiWarps); }
+    for (int w = 0; w < kEpiWarps; ++w) mbar_init(&aux_bar[w], 1);
     fence_barrier_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
@@ -245,28 +221,81 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
+    const int ew = warp - 2;                // epilogue warp index
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
-    const int half = (warp - 2) / 4;        // which half of the tile's columns
+    const int half = ew / 4;                // which half of the tile's columns
+    uint8_t* buf_o = staging + ew * 2 * kStageBufBytes;
+    uint8_t* buf_x = buf_o + kStageBufBytes;
+    const bool atomic = args.mode == kAtomicF32;
+    const bool need_aux = args.mode == kResidual || args.mode == kDRelu2;
+    uint32_t aux_phase = 0;
+    bool ok = true;
     int local = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++local) {
       int m, n, kb0, kb1;
       unit_coords(args, u, m, n, kb0, kb1);
       const int b = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&acc_full[b], acc_phase, kErrTimeoutEpilogue, args.err)) break;
       tc_fence_after();
-      const int row = m * BM + q * 32 + lane;
+      const int row0 = m * BM + q * 32;
 #pragma unroll 1
       for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+        const int col0 = n * BN + c * 32;
+        if (col0 >= args.N) break;  // uniform across the warp
+        if (need_aux && lane == 0) {
+          fence_proxy_async();  // earlier reads of buf_x precede the new load
+          mbar_arrive_expect_tx(&aux_bar[ew], kStageBufBytes);
+          tma_load_2d(buf_x, &tmX, &aux_bar[ew], col0, row0);
+        }
         float v[32];
         tmem_ld_32x32(tmem_base + (uint32_t(q * 32) << 16) + b * BN + c * 32, v);
-        const int col0 = n * BN + c * 32;
-        if (col0 < args.N) epilogue_chunk(args, row, col0, v);
+        if (atomic) {
+          atomic_chunk(args, row0 + lane, col0, v);
+          continue;
+        }
+        float x[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[i] = args.alpha * v[i];
+        if (need_aux) {
+          if (!mbar_wait(&aux_bar[ew], aux_phase, kErrTimeoutEpilogue, args.err)) { ok = false; break; }
+          aux_phase ^= 1;
+          float y[32];
+          stage_row_load(buf_x, lane, y);
+          if (args.mode == kDRelu2) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)  // d/dh relu(h)^2 = 2 relu(h), on the bf16-rounded upstream grad
+              x[i] = __bfloat162float(__float2bfloat16(x[i])) * 2.f * fmaxf(y[i], 0.f);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) x[i] = __bfloat162float(__float2bfloat16(x[i])) + y[i];
+          }
+        }
+        if (lane == 0) bulk_wait_read<0>();  // the previous chunk's stores have left the buffers
+        __syncwarp();
+        if (args.mode == kRelu2) {
+          stage_row_store(buf_x, lane, x);  // pre-activation h
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            // Square the bf16-rounded pre-activation, as relu(h)^2 on a bf16 h would.
+            const float hr = fmaxf(__bfloat162float(__float2bfloat16(x[i])), 0.f);
+            x[i] = hr * hr;
+          }
+        }
+        stage_row_store(buf_o, lane, x);
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, buf_o, col0, row0);
+          if (args.mode == kRelu2) tma_store_2d(&tmX, buf_x, col0, row0);
+          bulk_commit();
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
     }
+    if (lane == 0) bulk_wait<0>();
   }
   tc_fence_before();
   __syncthreads();
@@ -287,7 +316,8 @@ static int num_sms() {
 }
 
 template <int BN>
-static void launch(const GemmArgs& args, const CUtensorMap& ta, const CUtensorMap& tb, cudaStream_t stream) {
+static void launch(const GemmArgs& args, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                   const CUtensorMap& tx, cudaStream_t stream) {
   static bool configured = false;
   if (!configured) {
     TORCH_CHECK(cudaFuncSetAttribute(gemm_bf16_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -297,7 +327,7 @@ static void launch(const GemmArgs& args, const CUtensorMap& ta, const CUtensorMa
   }
   const int units = args.num_m * args.num_n * args.splits;
   const int grid = std::min(units, num_sms());
-  gemm_bf16_kernel<BN><<<grid, kThreads, Smem<BN>::kTotal, stream>>>(ta, tb, args);
+  gemm_bf16_kernel<BN><<<grid, kThreads, Smem<BN>::kTotal, stream>>>(ta, tb, tc, tx, args);
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "gemm launch failed");
 }
 
@@ -364,10 +394,19 @@ void gemm(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_major, to
                               : make_tmap_bf16_2d(A.data_ptr(), K, M, A.stride(0), 64, BM);
   CUtensorMap tb = b_mn_major ? make_tmap_bf16_2d(B.data_ptr(), N, K, B.stride(0), 64, 64)
                               : make_tmap_bf16_2d(B.data_ptr(), K, N, B.stride(0), 64, BN);
+  // Epilogue maps: 32 x 32 bf16 boxes, 64-byte swizzle (unused in the fp32 atomic mode).
+  CUtensorMap tc = ta, tx = ta;
+  if (!f32out) {
+    tc = make_tmap_bf16_2d_swz(C.data_ptr(), N, M, C.stride(0), 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (mode == kResidual || mode == kDRelu2)
+      tx = make_tmap_bf16_2d_swz(aux->data_ptr(), N, M, aux->stride(0), 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+    else if (mode == kRelu2)
+      tx = make_tmap_bf16_2d_swz(aux_out->data_ptr(), N, M, aux_out->stride(0), 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+  }
   const at::cuda::CUDAGuard guard(A.device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  if (BN == 128) launch<128>(args, ta, tb, stream);
-  else launch<256>(args, ta, tb, stream);
+  if (BN == 128) launch<128>(args, ta, tb, tc, tx, stream);
+  else launch<256>(args, ta, tb, tc, tx, stream);
 }
 
 }  // namespace nk
