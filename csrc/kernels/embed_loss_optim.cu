@@ -22,19 +22,27 @@ namespace nk {
 
 // ---- embedding --------------------------------------------------------------
 
-__global__ void embedding_fwd_kernel(const int64_t* __restrict__ idx, const float* __restrict__ wte,
+__device__ __forceinline__ uint2 embed_load4(const float* row, int c) {
+  const float4 f = reinterpret_cast<const float4*>(row)[c];
+  return make_uint2(pack_bf16x2(f.x, f.y), pack_bf16x2(f.z, f.w));
+}
+__device__ __forceinline__ uint2 embed_load4(const __nv_bfloat16* row, int c) {
+  return reinterpret_cast<const uint2*>(row)[c];
+}
+
+// The table is either the fp32 master or its bf16 working copy (identical
+// after rounding: the reference casts the gathered fp32 rows to bf16).
+template <typename T>
+__global__ void embedding_fwd_kernel(const int64_t* __restrict__ idx, const T* __restrict__ wte,
                                      __nv_bfloat16* __restrict__ out, int rows, int C, int V) {
   const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   if (row >= rows) return;
   const int64_t t = idx[row];
   if (t < 0 || t >= V) return;  // host validates ids; never read out of range
-  const float4* src = reinterpret_cast<const float4*>(wte + t * C);
+  const T* src = wte + t * C;
   uint2* dst = reinterpret_cast<uint2*>(out + long(row) * C);
-  for (int c = lane; c < C / 4; c += 32) {
-    float4 f = src[c];
-    dst[c] = make_uint2(pack_bf16x2(f.x, f.y), pack_bf16x2(f.z, f.w));
-  }
+  for (int c = lane; c < C / 4; c += 32) dst[c] = embed_load4(src, c);
 }
 
 __global__ void embedding_bwd_kernel(const int64_t* __restrict__ idx, const __nv_bfloat16* __restrict__ dx,
@@ -55,13 +63,21 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ idx, const __nv
 
 void embedding_fwd(torch::Tensor idx, torch::Tensor wte, torch::Tensor out) {
   TORCH_CHECK(idx.scalar_type() == at::kLong && idx.is_contiguous(), "embedding: int64 ids");
-  TORCH_CHECK(wte.scalar_type() == at::kFloat && wte.is_contiguous() && out.is_contiguous(), "embedding: layout");
+  TORCH_CHECK(wte.is_contiguous() && out.is_contiguous(), "embedding: layout");
   const int rows = int(idx.numel()), V = int(wte.size(0)), C = int(wte.size(1));
   TORCH_CHECK(C % 4 == 0 && out.numel() == int64_t(rows) * C, "embedding: shape");
   const at::cuda::CUDAGuard guard(idx.device());
   const int warps = 8;
-  embedding_fwd_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
-      idx.data_ptr<int64_t>(), wte.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rows, C, V);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  if (wte.scalar_type() == at::kFloat)
+    embedding_fwd_kernel<float><<<(rows + warps - 1) / warps, warps * 32, 0, stream>>>(
+        idx.data_ptr<int64_t>(), wte.data_ptr<float>(), op, rows, C, V);
+  else if (wte.scalar_type() == at::kBFloat16)
+    embedding_fwd_kernel<__nv_bfloat16><<<(rows + warps - 1) / warps, warps * 32, 0, stream>>>(
+        idx.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(wte.data_ptr()), op, rows, C, V);
+  else
+    TORCH_CHECK(false, "embedding: fp32 or bf16 table");
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "embedding_fwd launch failed");
 }
 

@@ -97,7 +97,7 @@ class FusedGpt:
         cfg, st = self.cfg, self.store
         b, t = idx.shape
         eps = cfg.norm_eps
-        x = L.embedding(idx, st.param("wte.weight"), out=ws.x[0])
+        x = L.embedding(idx, st.work_of("wte.weight"), out=ws.x[0])
         for i in range(cfg.n_layer):
             j = i if train else 0
             p = f"blocks.{i}."

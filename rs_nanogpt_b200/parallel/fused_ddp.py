@@ -1,0 +1,110 @@
+"""Fused data-parallel optimizer step (``--backend fused``).
+
+The flat fp32 gradient buffer and the flat bf16 working-weight buffer live in
+symmetric memory (``torch.distributed._symmetric_memory``: one allocation per
+rank, mapped into every peer over NVLink), which gives each rank device
+pointers to every peer's buffers. One step is then three of this package's
+kernels on the compute stream (``csrc/kernels/ddp_fused.cu``):
+
+1. signal-pad barrier: every rank's backward has finished writing gradients;
+2. ``ddp_rs_adam_ag``: for this rank's shard, sum the peers' gradients over
+   NVLink, apply the AdamW update of the parameter's group to the local fp32
+   master / m / v, and store the new bf16 weights into every peer's working
+   copy; the squared norm of the reduced gradient is accumulated on the way;
+3. signal-pad barrier: all peers have read this rank's gradients and written
+   its weights, so the next step may start.
+
+Mathematically this is DDP (gradient mean) followed by the reference's AdamW;
+only the summation order differs. The fp32 master weights and AdamW moments
+are sharded (each rank updates only its slice); ``gather_master`` rebuilds the
+full fp32 master when a checkpoint or a sample needs it.
+"""
+from typing import Optional
+
+import torch
+
+from ..ops._ext import ext
+from ..train.optim import BETAS, GroupedAdamW
+from .dist import DistCtx
+
+SHARD_ALIGN = 64
+
+
+class FusedDdp:
+    def __init__(self, store, opt: GroupedAdamW, dist: DistCtx):
+        import torch.distributed as td
+        import torch.distributed._symmetric_memory as symm
+
+        self.store, self.opt, self.dist = store, opt, dist
+        self.world, self.rank = dist.world_size(), dist.rank()
+        if self.world > 8:
+            raise ValueError("the fused DDP kernel supports up to 8 ranks (one NVSwitch node)")
+        group = td.group.WORLD
+        name = group.group_name
+        try:
+            symm.enable_symm_mem_for_group(name)
+        except Exception:  # newer torch enables it implicitly
+            pass
+        dev = store.device
+        total = store.total
+        grad = symm.empty(total, dtype=torch.float32, device=dev)
+        grad.zero_()
+        work = symm.empty(total, dtype=torch.bfloat16, device=dev)
+        work.copy_(store.work)
+        pads = symm.empty(16, dtype=torch.int32, device=dev)
+        pads.zero_()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        self.h_grad = symm.rendezvous(grad, name)
+        self.h_work = symm.rendezvous(work, name)
+        self.h_pads = symm.rendezvous(pads, name)
+        store.grad, store.work = grad, work
+        self._keep = (grad, work, pads)
+        shard = (total + self.world - 1) // self.world
+        self.shard = (shard + SHARD_ALIGN - 1) // SHARD_ALIGN * SHARD_ALIGN
+        self.lo = min(total, self.rank * self.shard)
+        self.hi = min(total, self.lo + self.shard)
+        self.epoch = 0
+        self.sumsq = torch.zeros(1, dtype=torch.float64, device=dev)
+        for lo, hi in opt.ranges.values():
+            assert lo % 4 == 0 and hi % 4 == 0, "parameter groups must be 4-element aligned"
+
+    def _barrier(self) -> None:
+        self.epoch += 1
+        ext().ddp_barrier(int(self.h_pads.buffer_ptrs_dev), self.rank, self.world, self.epoch)
+
+    def _groups(self) -> torch.Tensor:
+        opt = self.opt
+        t = opt.step_t
+        lrs = opt.current_lrs()
+        rows = []
+        for group, (lo, hi) in sorted(opt.ranges.items(), key=lambda kv: kv[1][0]):
+            b1, b2, eps = BETAS[group]
+            rows.append([lo, hi, getattr(lrs, group), b1, b2, eps, getattr(opt.wd, group),
+                         1.0 / (1.0 - b1 ** t), 1.0 / (1.0 - b2 ** t)])
+        return torch.tensor(rows, dtype=torch.float64)
+
+    def reduce_and_step(self, grad_scale: float = 1.0) -> None:
+        self.opt.step_t += 1
+        st = self.store
+        self._barrier()
+        self.sumsq.zero_()
+        ext().ddp_rs_adam_ag(int(self.h_grad.buffer_ptrs_dev), int(self.h_work.buffer_ptrs_dev), self.world,
+                             st.master, self.opt.m, self.opt.v, self.lo, self.hi, self._groups(),
+                             grad_scale / self.world, self.sumsq)
+        self._barrier()
+
+    def grad_norm(self) -> float:
+        """Norm of the reduced (mean) gradient of the last step, over all shards."""
+        return self.dist.all_reduce_sums([float(self.sumsq.item())])[0] ** 0.5
+
+    def gather_master(self) -> None:
+        """Make every rank's fp32 master complete again (after sharded updates)."""
+        import torch.distributed as td
+        st = self.store
+        pad = self.shard * self.world
+        full = torch.zeros(pad, dtype=torch.float32, device=st.device)
+        full[: st.total].copy_(st.master)
+        mine = full[self.rank * self.shard:(self.rank + 1) * self.shard].clone()
+        td.all_gather_into_tensor(full, mine)
+        st.master.copy_(full[: st.total])

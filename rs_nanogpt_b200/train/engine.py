@@ -98,6 +98,10 @@ class TrainEngine:
         return StepStats(nll_sum, count)
 
     def grad_norm(self) -> float:
+        """L2 norm of the step's (mean) gradient. Collective with --backend fused:
+        call it on every rank."""
+        if self.fused_ddp is not None:
+            return self.fused_ddp.grad_norm()
         st = self.store
         if st.device.type == "cuda":
             from ..ops import layers as L
@@ -105,6 +109,12 @@ class TrainEngine:
             L.sumsq(st.grad, out)
             return float(out.item()) ** 0.5
         return float(st.grad.double().pow(2).sum().item()) ** 0.5
+
+    def sync_master(self) -> None:
+        """Make the fp32 master weights complete on every rank (they are sharded
+        under --backend fused). Collective: call it on every rank."""
+        if self.fused_ddp is not None:
+            self.fused_ddp.gather_master()
 
     @torch.no_grad()
     def eval_nll(self, inputs: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:

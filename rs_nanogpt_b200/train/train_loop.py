@@ -127,10 +127,13 @@ def train(engine: TrainEngine, batches, cfg: TrainConfig, ev: EvalContext, fault
                 ev.metrics.log(step, "eval", time.perf_counter() - t_start, val_loss=m.val_loss, bpb=m.bpb)
             if m.bpb < best:
                 best = m.bpb
+                engine.sync_master()
                 if dist.is_master():
                     checkpoint.save(f"{ev.ckpt_root}/best", store,
                                     checkpoint.CheckpointMeta(store.cfg, step, m.bpb),
                                     engine.opt if ev.save_optimizer else None)
+        if cadence_fires(step, cfg.num_iters, ev.sample_every):
+            engine.sync_master()
         if dist.is_master() and cadence_fires(step, cfg.num_iters, ev.sample_every):
             opts = SampleOptions(ev.sample_tokens, ev.sample_temperature, 0, step)
             stops = ev.tokenizer.assistant_stop_ids() if ev.sample_chat else []
@@ -156,10 +159,10 @@ def train(engine: TrainEngine, batches, cfg: TrainConfig, ev: EvalContext, fault
             check_finite(mean_ce, step)
             if store.device.type == "cuda":
                 torch.cuda.synchronize()
+            gnorm = engine.grad_norm()
             now = time.perf_counter()
             if dist.is_master():
                 lrs = engine.opt.current_lrs()
-                gnorm = engine.grad_norm()
                 steps_in = step - win_step
                 elapsed = now - t_start
                 if steps_in > 0:

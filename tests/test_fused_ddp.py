@@ -1,0 +1,69 @@
+"""Fused reduce-scatter + AdamW + all-gather kernel vs the NCCL all-reduce
+baseline on 2 GPUs: identical data, identical init, the parameters must agree
+after several optimizer steps. Needs at least 2 GPUs (skipped otherwise)."""
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+SCRIPT = r"""
+import os, sys, torch
+from rs_nanogpt_b200.config import GptConfig
+from rs_nanogpt_b200.models.params import ParamStore, init_params
+from rs_nanogpt_b200.ops._ext import kernel_status
+from rs_nanogpt_b200.parallel.dist import DistCtx, child_env
+from rs_nanogpt_b200.train.engine import TrainEngine
+from rs_nanogpt_b200.train.optim import GroupLrs
+env = child_env()
+torch.cuda.set_device(env.local_rank)
+dev = torch.device("cuda", env.local_rank)
+dist = DistCtx.init(env, "nccl", dev)
+cfg = GptConfig(vocab_size=1024, sequence_len=128, n_layer=2, n_head=2, n_embd=256, rope_base=10000.0)
+engines = {}
+for backend in ("nccl", "fused"):
+    st = ParamStore(cfg, dev)
+    init_params(st, seed=5, mode="bench")
+    g = torch.Generator(device=dev).manual_seed(9)
+    for n in st.names():
+        if n.endswith("c_proj.weight"):
+            st.param(n).normal_(0, 0.02, generator=g)
+    st.refresh_work()
+    engines[backend] = TrainEngine(st, GroupLrs(0.2, 0.004, 0.003), dist=dist, comm=backend)
+g = torch.Generator(device=dev).manual_seed(100 + dist.rank())
+batches = []
+for _ in range(3):
+    x = torch.randint(0, 1024, (2, 129), device=dev, generator=g)
+    batches.append((x[:, :-1].contiguous(), x[:, 1:].contiguous()))
+norms = {}
+for backend, eng in engines.items():
+    for step, b in enumerate(batches):
+        eng.step([b], 256, 1.0 if step else 0.5)
+    norms[backend] = eng.grad_norm()
+    eng.sync_master()
+torch.cuda.synchronize()
+a, b = engines["nccl"].store, engines["fused"].store
+diff = (a.master - b.master).abs().max().item()
+wdiff = (a.work.float() - b.work.float()).abs().max().item()
+print(f"rank {dist.rank()} master diff {diff:.3e} work diff {wdiff:.3e} norms {norms}", flush=True)
+assert kernel_status() == 0
+assert diff < 2e-3, diff
+assert wdiff < 2e-2, wdiff
+assert abs(norms["nccl"] - norms["fused"]) < 1e-3 * max(1.0, norms["nccl"])
+dist.shutdown()
+os._exit(0)
+"""
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fused_ddp_matches_nccl_baseline(tmp_path):
+    from rs_nanogpt_b200.parallel.launcher import spawn_ranks, supervise_ranks
+    script = tmp_path / "ddp.py"
+    script.write_text(SCRIPT)
+    env = {"PYTHONPATH": ROOT + os.pathsep + os.environ.get("PYTHONPATH", "")}
+    assert supervise_ranks(spawn_ranks(2, [sys.executable, str(script)], env)) == 0
