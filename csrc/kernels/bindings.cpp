@@ -27,6 +27,8 @@ void ddp_barrier(int64_t pads_dev, int64_t rank, int64_t world, int64_t epoch);
 void ddp_rs_adam_ag(int64_t grads_dev, int64_t works_dev, int64_t world, torch::Tensor master, torch::Tensor m,
                     torch::Tensor v, int64_t shard_lo, int64_t shard_hi, torch::Tensor groups, double grad_scale,
                     c10::optional<torch::Tensor> sumsq);
+void flash_fwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor lse, int64_t B, int64_t T, int64_t H);
+bool flash_fwd_tc_supported(int64_t T, int64_t HD);
 }  // namespace nk
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -46,6 +48,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sumsq", &nk::sumsq);
   m.def("flash_fwd", &nk::flash_fwd);
   m.def("flash_bwd", &nk::flash_bwd);
+  m.def("flash_fwd_tc", &nk::flash_fwd_tc);
+  m.def("flash_fwd_tc_supported", &nk::flash_fwd_tc_supported);
   m.def("ddp_barrier", &nk::ddp_barrier);
   m.def("ddp_rs_adam_ag", &nk::ddp_rs_adam_ag);
 }

@@ -1,0 +1,306 @@
+// Causal flash-attention forward on the 5th-generation tensor cores
+// (tcgen05 + TMEM + TMA), head_dim 128, seq_len a multiple of 256.
+//
+// One CTA = two 128-row query tiles of one (batch, head); key/value blocks of
+// 128. TMEM (512 columns) holds S0, S1 (scores of the two tiles) and O0, O1
+// (their output accumulators). Roles:
+//   warp 0      TMA loads: Q0, Q1 once, then K_j and V_j per key block
+//               (3-D tensor map over the fused QKV buffer; no multicast)
+//   warp 1      TMEM allocation + single-thread MMA issue:
+//               S_t = Q_t K_j^T, then O_t += P_t V_j
+//   warps 2-5   softmax for tile 0, warps 6-9 for tile 1: thread = query row.
+//               Reads its S row from TMEM, applies the causal mask on the
+//               diagonal block, keeps the running max / sum in registers,
+//               writes P (bf16) to shared memory in the UMMA K-major swizzled
+//               layout, and rescales its O row in TMEM only when the row max
+//               grew by more than 2^8 since the last rescale (otherwise the
+//               stale max is kept, which only scales P and O by the same
+//               bounded factor).
+// Two tiles per CTA let the tensor core compute one tile's MMAs while the
+// other tile's softmax runs.
+//
+// Output and LSE conventions match flash_attn.cu (LSE in base-2 units of the
+// scaled scores), so the backward kernels consume either forward's results.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+#include "status.h"
+#include "tma_host.h"
+
+namespace nk {
+
+namespace fa {
+constexpr int HD = 128, BM = 128, BN = 128;
+constexpr int kThreads = 320;
+constexpr int kTileBytes = BM * HD * 2;      // 32 KB: Q tile, K block, V block or P tile
+constexpr int kSubBytes = 128 * 64 * 2;      // 16 KB: one 64-column swizzle sub-tile
+constexpr int kSmem = 6 * kTileBytes + 1024 + 256;
+constexpr float kRescaleThreshold = 8.0f;    // log2 units
+}  // namespace fa
+
+struct FaArgs {
+  __nv_bfloat16* out;
+  long ld_out;
+  float* lse;
+  int B, H, T, C;
+  float sl2;
+  int* err;
+};
+
+// P tile staging: row r, 16-byte chunk c (8 keys) of the 128 keys; sub-tile
+// c / 8 covers keys [64 * (c / 8), +64), each row 128 B, 128B-swizzled.
+__device__ __forceinline__ uint32_t p_off(int r, int c) {
+  return uint32_t((c >> 3) * fa::kSubBytes + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+__global__ void __launch_bounds__(fa::kThreads, 1)
+    flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm, const FaArgs a) {
+  using namespace fa;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                       // 2 tiles
+  uint8_t* sK = smem + 2 * kTileBytes;
+  uint8_t* sV = smem + 3 * kTileBytes;
+  uint8_t* sP = smem + 4 * kTileBytes;      // 2 tiles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTileBytes);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = bars + 2;
+  uint64_t* v_full = bars + 3;
+  uint64_t* v_empty = bars + 4;
+  uint64_t* s_full = bars + 5;   // [2]
+  uint64_t* p_full = bars + 7;   // [2]
+  uint64_t* o_done = bars + 9;   // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int qb = gridDim.x - 1 - blockIdx.x;  // longest rows first
+  const int b = blockIdx.y / a.H, h = blockIdx.y % a.H;
+  const int q0 = qb * 2 * BM;
+  const int nblk1 = (q0 + 2 * BM) / BN;       // key blocks of tile 1; tile 0 has one fewer
+  const int xq = h * HD, xk = a.C + h * HD, xv = 2 * a.C + h * HD;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(k_full, 1);
+    mbar_init(k_empty, 1);
+    mbar_init(v_full, 1);
+    mbar_init(v_empty, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&o_done[t], 1);
+    }
+    fence_barrier_init();
+    prefetch_tmap(&tm);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;  // S0 @0, S1 @128, O0 @256, O1 @384
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
+      for (int t = 0; t < 2; ++t)
+        for (int s = 0; s < 2; ++s)
+          tma_load_3d(sQ + t * kTileBytes + s * kSubBytes, &tm, q_full, xq + 64 * s, q0 + t * BM, b);
+      for (int j = 0; j < nblk1; ++j) {
+        const uint32_t ph = j & 1;
+        if (!mbar_wait(k_empty, ph ^ 1, kErrTimeoutProducer, a.err)) break;
+        mbar_arrive_expect_tx(k_full, kTileBytes);
+        for (int s = 0; s < 2; ++s) tma_load_3d(sK + s * kSubBytes, &tm, k_full, xk + 64 * s, j * BN, b);
+        if (!mbar_wait(v_empty, ph ^ 1, kErrTimeoutProducer, a.err)) break;
+        mbar_arrive_expect_tx(v_full, kTileBytes);
+        for (int s = 0; s < 2; ++s) tma_load_3d(sV + s * kSubBytes, &tm, v_full, xv + 64 * s, j * BN, b);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id_s = idesc_bf16(BM, BN, false, false);  // Q K^T: both K-major
+      const uint32_t id_o = idesc_bf16(BM, HD, false, true);   // P V: V is MN-major (d contiguous)
+      bool ok = mbar_wait(q_full, 0, kErrTimeoutMma, a.err);
+      for (int j = 0; j < nblk1 && ok; ++j) {
+        const uint32_t ph = j & 1;
+        if (!mbar_wait(k_full, ph, kErrTimeoutMma, a.err)) break;
+        tc_fence_after();
+        for (int t = 0; t < 2; ++t) {
+          if (j >= nblk1 - 1 + t) continue;  // tile 0 skips the last key block
+          if (j > 0 && !mbar_wait(&p_full[t], (j - 1) & 1, kErrTimeoutMma, a.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t q = smem_u32(sQ + t * kTileBytes), k = smem_u32(sK);
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * kSubBytes + (kk & 3) * 32;
+            umma_bf16(tmem + t * BN, sw128_desc(q + off, 16, 1024), sw128_desc(k + off, 16, 1024), id_s,
+                      kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[t]);
+        }
+        if (!ok) break;
+        umma_commit(k_empty);
+        if (!mbar_wait(v_full, ph, kErrTimeoutMma, a.err)) break;
+        tc_fence_after();
+        for (int t = 0; t < 2; ++t) {
+          if (j >= nblk1 - 1 + t) continue;
+          if (!mbar_wait(&p_full[t], j & 1, kErrTimeoutMma, a.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t p = smem_u32(sP + t * kTileBytes), v = smem_u32(sV);
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const uint32_t poff = (kk >> 2) * kSubBytes + (kk & 3) * 32;
+            umma_bf16(tmem + 256 + t * HD, sw128_desc(p + poff, 16, 1024), sw128_desc(v + kk * 2048, kSubBytes, 1024),
+                      id_o, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&o_done[t]);
+        }
+        if (!ok) break;
+        umma_commit(v_empty);
+      }
+    }
+  } else {
+    // Softmax warpgroups.
+    const int t = (warp - 2) / 4;                  // query tile
+    const int quarter = warp & 3;                  // TMEM lanes this warp may access
+    const int r = quarter * 32 + lane;             // row within the tile
+    const int qrow = q0 + t * BM + r;              // absolute query position
+    const int nblk = nblk1 - 1 + t;
+    const uint32_t t_s = tmem + (uint32_t(quarter * 32) << 16) + t * BN;
+    const uint32_t t_o = tmem + (uint32_t(quarter * 32) << 16) + 256 + t * HD;
+    uint8_t* P = sP + t * kTileBytes;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nblk && ok; ++j) {
+      if (!mbar_wait(&s_full[t], j & 1, kErrTimeoutEpilogue, a.err)) { ok = false; break; }
+      tc_fence_after();
+      const bool diag = j == nblk - 1;
+      // Pass 1: row max of the scaled scores.
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        tmem_ld_32x32(t_s + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int key = j * BN + c * 32 + i;
+          const float s = (diag && key > qrow) ? -INFINITY : v[i] * a.sl2;
+          mx = fmaxf(mx, s);
+        }
+      }
+      // The previous P V must be done before P is rewritten or O rescaled.
+      if (j > 0 && !mbar_wait(&o_done[t], (j - 1) & 1, kErrTimeoutEpilogue, a.err)) { ok = false; break; }
+      tc_fence_after();
+      const bool grow = mx > m_used + kRescaleThreshold;
+      if (__any_sync(0xffffffffu, grow)) {
+        const float m_new = grow ? mx : m_used;
+        const float alpha = exp2f(m_used - m_new);  // 0 on the first block, 1 for rows that keep their max
+        if (j > 0) {
+#pragma unroll 1
+          for (int c = 0; c < HD / 32; ++c) {
+            float o[32];
+            tmem_ld_32x32(t_o + c * 32, o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tmem_st_32x32(t_o + c * 32, o);
+          }
+        }
+        l *= alpha;
+        m_used = m_new;
+      }
+      // Pass 2: P = exp2(s - m_used) -> bf16 in shared memory.
+      float rs = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        tmem_ld_32x32(t_s + c * 32, v);
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const int key = j * BN + c * 32 + i;
+          const float p0 = (diag && key > qrow) ? 0.f : exp2f(v[i] * a.sl2 - m_used);
+          const float p1 = (diag && key + 1 > qrow) ? 0.f : exp2f(v[i + 1] * a.sl2 - m_used);
+          rs += p0 + p1;
+          pk[i / 2] = pack_bf16x2(p0, p1);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(P + p_off(r, c * 4 + q)) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2],
+                                                                           pk[4 * q + 3]);
+      }
+      l += rs;
+      fence_proxy_async();  // generic-proxy smem writes -> visible to the tensor core
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
+    }
+    if (ok && mbar_wait(&o_done[t], (nblk - 1) & 1, kErrTimeoutEpilogue, a.err)) {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      __nv_bfloat16* orow = a.out + (long(b) * a.T + qrow) * a.ld_out + h * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
+        float o[32];
+        tmem_ld_32x32(t_o + c * 32, o);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(orow + c * 32 + q * 8) =
+              make_uint4(pack_bf16x2(o[8 * q] * inv, o[8 * q + 1] * inv), pack_bf16x2(o[8 * q + 2] * inv, o[8 * q + 3] * inv),
+                         pack_bf16x2(o[8 * q + 4] * inv, o[8 * q + 5] * inv), pack_bf16x2(o[8 * q + 6] * inv, o[8 * q + 7] * inv));
+      }
+      a.lse[(long(b) * a.H + h) * a.T + qrow] = m_used + log2f(l);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+bool flash_fwd_tc_supported(int64_t T, int64_t HD) { return HD == 128 && T % 256 == 0; }
+
+// qkv: (B*T, 3C) bf16; out: (B*T, C) bf16; lse: (B, H, T) fp32.
+void flash_fwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor lse, int64_t B, int64_t T, int64_t H) {
+  using namespace fa;
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.is_contiguous(), "flash_tc: contiguous bf16 qkv");
+  const int64_t C = qkv.size(1) / 3;
+  TORCH_CHECK(C == H * HD && qkv.size(0) == B * T && flash_fwd_tc_supported(T, C / H), "flash_tc: shape");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.stride(1) == 1 && out.size(1) == C &&
+                  (out.stride(0) * 2) % 16 == 0 && reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
+              "flash_tc: out");
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.numel() == B * H * T, "flash_tc: lse");
+  // 3-D map (inner: 3C columns, then T rows of one sequence, then B sequences):
+  // rows past a sequence's end read as zeros instead of the next sequence.
+  CUtensorMap m;
+  cuuint64_t dims[3] = {cuuint64_t(3 * C), cuuint64_t(T), cuuint64_t(B)};
+  cuuint64_t strides[2] = {cuuint64_t(3 * C * 2), cuuint64_t(T * 3 * C * 2)};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_tiled_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, qkv.data_ptr(), dims, strides, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "flash_tc: tensor map encode failed ", int(r));
+  FaArgs a{};
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.ld_out = out.stride(0);
+  a.lse = lse.data_ptr<float>();
+  a.B = int(B); a.H = int(H); a.T = int(T); a.C = int(C);
+  a.sl2 = (1.f / std::sqrt(float(HD))) * 1.4426950408889634f;
+  a.err = error_word();
+  static bool configured = false;
+  if (!configured) {
+    TORCH_CHECK(cudaFuncSetAttribute(flash_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) ==
+                    cudaSuccess, "flash_tc: smem");
+    configured = true;
+  }
+  const at::cuda::CUDAGuard guard(qkv.device());
+  dim3 grid(unsigned(T / 256), unsigned(B * H));
+  flash_fwd_tc_kernel<<<grid, kThreads, kSmem, at::cuda::getCurrentCUDAStream()>>>(m, a);
+  TORCH_CHECK(cudaGetLastError() == cudaSuccess, "flash_fwd_tc launch failed");
+}
+
+}  // namespace nk

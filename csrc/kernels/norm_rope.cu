@@ -131,10 +131,18 @@ void rmsnorm_fwd(torch::Tensor x, torch::Tensor y, c10::optional<torch::Tensor> 
   const int warps = 8, grid = (rows + warps - 1) / warps;
   auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
   auto yp = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
-  if (C <= 1024)
-    rmsnorm_fwd_kernel<4><<<grid, warps * 32, 0, stream>>>(xp, yp, r, rows, C, x.stride(0), y.stride(0), float(eps));
-  else
-    rmsnorm_fwd_kernel<8><<<grid, warps * 32, 0, stream>>>(xp, yp, r, rows, C, x.stride(0), y.stride(0), float(eps));
+  // Vectors of 8 per lane: the template bound is the smallest that covers C,
+  // so no registers are spent on lanes that never load.
+  const int vpt = (C / 8 + 31) / 32;
+#define RMS_FWD(N) rmsnorm_fwd_kernel<N><<<grid, warps * 32, 0, stream>>>(xp, yp, r, rows, C, x.stride(0), \
+                                                                             y.stride(0), float(eps))
+  if (vpt <= 2) RMS_FWD(2);
+  else if (vpt <= 3) RMS_FWD(3);
+  else if (vpt <= 4) RMS_FWD(4);
+  else if (vpt <= 5) RMS_FWD(5);
+  else if (vpt <= 6) RMS_FWD(6);
+  else RMS_FWD(8);
+#undef RMS_FWD
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "rmsnorm_fwd launch failed");
 }
 
@@ -150,10 +158,16 @@ void rmsnorm_bwd(torch::Tensor x, torch::Tensor dy, torch::Tensor rstd, torch::T
   auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
   auto gp = reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr());
   auto dp = reinterpret_cast<__nv_bfloat16*>(dx.data_ptr());
-  if (C <= 1024)
-    rmsnorm_bwd_kernel<4><<<grid, warps * 32, 0, stream>>>(xp, gp, rstd.data_ptr<float>(), dp, rows, C, accum);
-  else
-    rmsnorm_bwd_kernel<8><<<grid, warps * 32, 0, stream>>>(xp, gp, rstd.data_ptr<float>(), dp, rows, C, accum);
+  const int vpt = (C / 8 + 31) / 32;
+#define RMS_BWD(N) rmsnorm_bwd_kernel<N><<<grid, warps * 32, 0, stream>>>(xp, gp, rstd.data_ptr<float>(), dp, rows, \
+                                                                             C, accum)
+  if (vpt <= 2) RMS_BWD(2);
+  else if (vpt <= 3) RMS_BWD(3);
+  else if (vpt <= 4) RMS_BWD(4);
+  else if (vpt <= 5) RMS_BWD(5);
+  else if (vpt <= 6) RMS_BWD(6);
+  else RMS_BWD(8);
+#undef RMS_BWD
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "rmsnorm_bwd launch failed");
 }
 

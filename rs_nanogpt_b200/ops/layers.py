@@ -60,8 +60,14 @@ def sumsq(x: torch.Tensor, out: torch.Tensor) -> None:
     ext().sumsq(x, out)
 
 
-def flash_attention(qkv, out, lse, batch: int, seq_len: int, n_head: int) -> None:
-    ext().flash_fwd(qkv, out, lse, batch, seq_len, n_head)
+def flash_attention(qkv, out, lse, batch: int, seq_len: int, n_head: int, impl: str = "auto") -> None:
+    """Causal attention forward. ``auto`` uses the tcgen05 kernel when the shape
+    allows it (head_dim 128, seq_len a multiple of 256), else the mma.sync one."""
+    hd = qkv.shape[1] // 3 // n_head
+    if impl == "tc" or (impl == "auto" and ext().flash_fwd_tc_supported(seq_len, hd)):
+        ext().flash_fwd_tc(qkv, out, lse, batch, seq_len, n_head)
+    else:
+        ext().flash_fwd(qkv, out, lse, batch, seq_len, n_head)
 
 
 def flash_attention_bwd(qkv, out, dout, lse, dsum, dqkv, batch: int, seq_len: int, n_head: int) -> None:

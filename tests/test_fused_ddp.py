@@ -40,10 +40,16 @@ batches = []
 for _ in range(3):
     x = torch.randint(0, 1024, (2, 129), device=dev, generator=g)
     batches.append((x[:, :-1].contiguous(), x[:, 1:].contiguous()))
+# Identical non-trivial optimizer state, then ONE step each: the split-K
+# weight gradients use fp32 atomics, so multi-step runs are not bitwise
+# reproducible and Adam would amplify that noise on near-zero gradients.
 norms = {}
 for backend, eng in engines.items():
-    for step, b in enumerate(batches):
-        eng.step([b], 256, 1.0 if step else 0.5)
+    gm = torch.Generator(device=dev).manual_seed(77)
+    eng.opt.m.copy_(torch.randn(eng.opt.m.shape, device=dev, generator=gm) * 1e-3)
+    eng.opt.v.copy_(torch.rand(eng.opt.v.shape, device=dev, generator=gm) * 1e-5)
+    eng.opt.step_t = 4
+    eng.step(batches[:2], 512, 0.7)
     norms[backend] = eng.grad_norm()
     eng.sync_master()
 torch.cuda.synchronize()
@@ -52,8 +58,8 @@ diff = (a.master - b.master).abs().max().item()
 wdiff = (a.work.float() - b.work.float()).abs().max().item()
 print(f"rank {dist.rank()} master diff {diff:.3e} work diff {wdiff:.3e} norms {norms}", flush=True)
 assert kernel_status() == 0
-assert diff < 2e-3, diff
-assert wdiff < 2e-2, wdiff
+assert diff < 1e-5, diff
+assert wdiff < 1e-2, wdiff
 assert abs(norms["nccl"] - norms["fused"]) < 1e-3 * max(1.0, norms["nccl"])
 dist.shutdown()
 os._exit(0)

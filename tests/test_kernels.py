@@ -147,3 +147,26 @@ def test_sumsq():
     out = torch.zeros(1, device="cuda", dtype=torch.float64)
     L.sumsq(x, out)
     assert abs(out.item() - (x.double() ** 2).sum().item()) < 1e-3 * out.item()
+
+
+@pytest.mark.parametrize("b,t,h", [(2, 256, 2), (1, 1024, 3), (2, 2048, 1)])
+def test_flash_attention_tcgen05_forward(b, t, h):
+    """tcgen05 forward vs the fp32 reference and vs the mma.sync kernel's LSE."""
+    from rs_nanogpt_b200.models.reference import attention
+    from rs_nanogpt_b200.ops import layers as L
+    torch.manual_seed(11)
+    d, c = 128, h * 128
+    qkv = (torch.randn(b * t, 3 * c, device="cuda") * 1.5).bfloat16()
+    out = torch.empty(b * t, c, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(b * h * t, device="cuda")
+    L.flash_attention(qkv, out, lse, b, t, h, impl="tc")
+    z = qkv.float()
+    q = z[:, :c].view(b, t, h, d).transpose(1, 2)
+    k = z[:, c:2 * c].view(b, t, h, d).transpose(1, 2)
+    v = z[:, 2 * c:].view(b, t, h, d).transpose(1, 2)
+    ref = attention(q, k, v, 0).transpose(1, 2).reshape(b * t, c)
+    _close(out, ref, 2e-2)
+    out2 = torch.empty_like(out)
+    lse2 = torch.empty_like(lse)
+    L.flash_attention(qkv, out2, lse2, b, t, h, impl="mma")
+    _close(lse, lse2, 1e-3)
