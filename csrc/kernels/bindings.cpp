@@ -29,6 +29,9 @@ void ddp_rs_adam_ag(int64_t grads_dev, int64_t works_dev, int64_t world, torch::
                     c10::optional<torch::Tensor> sumsq);
 void flash_fwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor lse, int64_t B, int64_t T, int64_t H);
 bool flash_fwd_tc_supported(int64_t T, int64_t HD);
+void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch::Tensor lse, torch::Tensor dsum,
+                  torch::Tensor dq_acc, torch::Tensor dqkv, int64_t B, int64_t T, int64_t H);
+bool flash_bwd_tc_supported(int64_t T, int64_t HD);
 }  // namespace nk
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -49,6 +52,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_fwd", &nk::flash_fwd);
   m.def("flash_bwd", &nk::flash_bwd);
   m.def("flash_fwd_tc", &nk::flash_fwd_tc);
+  m.def("flash_bwd_tc", &nk::flash_bwd_tc);
+  m.def("flash_bwd_tc_supported", &nk::flash_bwd_tc_supported);
   m.def("flash_fwd_tc_supported", &nk::flash_fwd_tc_supported);
   m.def("ddp_barrier", &nk::ddp_barrier);
   m.def("ddp_rs_adam_ag", &nk::ddp_rs_adam_ag);

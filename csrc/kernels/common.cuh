@@ -183,6 +183,13 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Untiled bulk copy global -> shared (size and both addresses 16-byte aligned).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 // Shared-memory matrix descriptor for a 128-byte-swizzled bf16 tile.
 //  K-major : rows of 64 elements (128 B); SBO = 1024 B between 8-row groups.
 //  MN-major: 64-element MN blocks of K rows; LBO = byte stride between MN

@@ -551,6 +551,26 @@ void flash_bwd(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch::
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "flash_bwd launch failed");
 }
 
+// D = rowsum(dO o O) alone (used by the tcgen05 backward).
+void flash_dsum(torch::Tensor out, torch::Tensor dout, torch::Tensor dsum, int64_t B, int64_t T, int64_t H) {
+  const int64_t C = out.size(1);
+  const int HD = int(C / H);
+  TORCH_CHECK(HD == 64 || HD == 128, "flash_dsum: head_dim");
+  TORCH_CHECK(out.stride(1) == 1 && dout.stride(1) == 1 && dsum.numel() == B * H * T, "flash_dsum: shapes");
+  AttnArgs d{};
+  d.o = reinterpret_cast<const __nv_bfloat16*>(out.data_ptr());
+  d.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
+  d.ld_out = out.stride(0);
+  d.ld_do = dout.stride(0);
+  d.dsum = dsum.data_ptr<float>();
+  d.B = int(B); d.H = int(H); d.T = int(T);
+  const long items = B * T * H;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (HD == 128) flash_bwd_dot_kernel<128><<<unsigned((items + 7) / 8), 256, 0, stream>>>(d);
+  else flash_bwd_dot_kernel<64><<<unsigned((items + 7) / 8), 256, 0, stream>>>(d);
+  TORCH_CHECK(cudaGetLastError() == cudaSuccess, "flash_dsum launch failed");
+}
+
 }  // namespace nk
 
 // ---------------------------------------------------------------------------------------------

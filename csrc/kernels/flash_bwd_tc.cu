@@ -1,0 +1,350 @@
+// Causal flash-attention backward on the 5th-generation tensor cores
+// (tcgen05 + TMEM + TMA), head_dim 128, seq_len a multiple of 128.
+//
+// One CTA = one block of 128 keys of one (batch, head). K and V stay in
+// shared memory; for every query block j >= the key block (causal) it
+//   MMA1  S^T  = K  Q_j^T            -> TMEM [0,128)
+//   MMA2  dP^T = V  dO_j^T           -> TMEM [128,256)
+//   (compute warpgroup, thread = key row)
+//         P^T  = exp2(S^T * scale*log2e - lse2[q])   (causal mask on the diagonal)
+//         dS^T = P^T o (dP^T - D[q])                 both bf16 -> shared memory
+//   MMA3  dV  += P^T  dO_j           -> TMEM [384,512)
+//   MMA4  dK  += dS^T Q_j            -> TMEM [256,384)
+//   MMA5  dQ_j = dS K                -> TMEM [128,256) (dS^T's smem tile read as
+//                                       an MN-major A operand: no transpose copy)
+//   (drain warpgroup, thread = query row) dQ_j * scale is added to an fp32
+//   accumulator with vector atomics.
+// After the last block the compute warpgroup writes dK * scale and dV (bf16)
+// into the gradient buffer. A final small kernel converts the dQ accumulator
+// to bf16.
+//
+// Warps: 0 = TMA/bulk loads, 1 = TMEM allocation + MMA issue, 2-5 = compute,
+// 6-9 = dQ drain. Every wait is bounded (common.cuh).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+#include "status.h"
+#include "tma_host.h"
+
+namespace nk {
+
+namespace fb {
+constexpr int HD = 128, BK = 128, BQ = 128;
+constexpr int kThreads = 320;
+constexpr int kTile = 128 * 128 * 2;   // 32 KB
+constexpr int kSub = 128 * 64 * 2;     // 16 KB swizzle sub-tile
+constexpr int kSmem = 6 * kTile + 2 * BQ * 4 + 1024 + 256;
+}  // namespace fb
+
+struct FbArgs {
+  __nv_bfloat16* dqkv;  // (B*T, 3C): dK / dV written here
+  float* dq_acc;        // (B*T, C) fp32, zeroed by the host
+  const float* lse;     // (B, H, T) base-2
+  const float* dsum;    // (B, H, T)
+  int B, H, T, C;
+  float scale, sl2;
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t tile_off(int r, int c) {  // 16B chunk c (of 16) in row r, K-major SW128
+  return uint32_t((c >> 3) * fb::kSub + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+__global__ void __launch_bounds__(fb::kThreads, 1)
+    flash_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tmo,
+                        const FbArgs a) {
+  using namespace fb;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = smem + kTile;
+  uint8_t* sQ = smem + 2 * kTile;
+  uint8_t* sO = smem + 3 * kTile;   // dO_j
+  uint8_t* sP = smem + 4 * kTile;   // P^T  [key][query]
+  uint8_t* sS = smem + 5 * kTile;   // dS^T [key][query]
+  float* sL = reinterpret_cast<float*>(smem + 6 * kTile);  // lse2 of the query block
+  float* sD = sL + BQ;                                     // D of the query block
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTile + 2 * BQ * 4);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qd_full = bars + 1;
+  uint64_t* qd_empty = bars + 2;
+  uint64_t* st_full = bars + 3;
+  uint64_t* p_full = bars + 4;
+  uint64_t* dq_full = bars + 5;
+  uint64_t* dq_free = bars + 6;
+  uint64_t* kv_done = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int kb = blockIdx.x;  // key block; low blocks have the most query blocks
+  const int b = blockIdx.y / a.H, h = blockIdx.y % a.H;
+  const int nq = a.T / BQ;
+  const int nblk = nq - kb;   // query blocks kb .. nq-1
+  const long bh = long(b) * a.H + h;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(qd_full, 1);
+    mbar_init(qd_empty, 1);
+    mbar_init(st_full, 1);
+    mbar_init(p_full, 4);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 4);
+    mbar_init(kv_done, 1);
+    fence_barrier_init();
+    prefetch_tmap(&tm);
+    prefetch_tmap(&tmo);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;  // S^T @0, dP^T / dQ @128, dK @256, dV @384
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const int xq = h * HD, xk = a.C + h * HD, xv = 2 * a.C + h * HD;
+      mbar_arrive_expect_tx(kv_full, 2 * kTile);
+      for (int s = 0; s < 2; ++s) {
+        tma_load_3d(sK + s * kSub, &tm, kv_full, xk + 64 * s, kb * BK, b);
+        tma_load_3d(sV + s * kSub, &tm, kv_full, xv + 64 * s, kb * BK, b);
+      }
+      for (int n = 0; n < nblk; ++n) {
+        const int j = kb + n;
+        if (n > 0 && !mbar_wait(qd_empty, (n - 1) & 1, kErrTimeoutProducer, a.err)) break;
+        mbar_arrive_expect_tx(qd_full, 2 * kTile + 2 * BQ * 4);
+        for (int s = 0; s < 2; ++s) {
+          tma_load_3d(sQ + s * kSub, &tm, qd_full, xq + 64 * s, j * BQ, b);
+          tma_load_3d(sO + s * kSub, &tmo, qd_full, h * HD + 64 * s, j * BQ, b);
+        }
+        bulk_load(sL, a.lse + bh * a.T + j * BQ, BQ * 4, qd_full);
+        bulk_load(sD, a.dsum + bh * a.T + j * BQ, BQ * 4, qd_full);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id_kk = idesc_bf16(128, 128, false, false);  // MMA1, MMA2
+      const uint32_t id_kn = idesc_bf16(128, HD, false, true);    // MMA3, MMA4: B MN-major
+      const uint32_t id_nn = idesc_bf16(128, HD, true, true);     // MMA5: A and B MN-major
+      const uint32_t k = smem_u32(sK), v = smem_u32(sV), q = smem_u32(sQ), o = smem_u32(sO);
+      const uint32_t p = smem_u32(sP), ds = smem_u32(sS);
+      bool ok = mbar_wait(kv_full, 0, kErrTimeoutMma, a.err);
+      for (int n = 0; n < nblk && ok; ++n) {
+        if (!mbar_wait(qd_full, n & 1, kErrTimeoutMma, a.err)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kSub + (kk & 3) * 32;
+          umma_bf16(tmem + 0, sw128_desc(k + off, 16, 1024), sw128_desc(q + off, 16, 1024), id_kk, kk > 0);
+        }
+        // dP^T reuses the columns of the previous dQ: wait until it was drained.
+        if (n > 0 && !mbar_wait(dq_free, (n - 1) & 1, kErrTimeoutMma, a.err)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kSub + (kk & 3) * 32;
+          umma_bf16(tmem + 128, sw128_desc(v + off, 16, 1024), sw128_desc(o + off, 16, 1024), id_kk, kk > 0);
+        }
+        umma_commit(st_full);
+        if (!mbar_wait(p_full, n & 1, kErrTimeoutMma, a.err)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk) {  // contraction over the 128 queries
+          const uint32_t aoff = (kk >> 2) * kSub + (kk & 3) * 32;
+          umma_bf16(tmem + 384, sw128_desc(p + aoff, 16, 1024), sw128_desc(o + kk * 2048, kSub, 1024), id_kn,
+                    (n > 0 || kk > 0) ? 1u : 0u);
+          umma_bf16(tmem + 256, sw128_desc(ds + aoff, 16, 1024), sw128_desc(q + kk * 2048, kSub, 1024), id_kn,
+                    (n > 0 || kk > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {  // contraction over the 128 keys
+          umma_bf16(tmem + 128, sw128_desc(ds + kk * 2048, kSub, 1024), sw128_desc(k + kk * 2048, kSub, 1024),
+                    id_nn, kk > 0);
+        }
+        umma_commit(dq_full);
+        umma_commit(qd_empty);
+      }
+      umma_commit(kv_done);
+    }
+  } else if (warp < 6) {
+    // Compute warpgroup: thread = key row.
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int key = kb * BK + r;
+    const uint32_t lanes = uint32_t(quarter * 32) << 16;
+    bool ok = true;
+    for (int n = 0; n < nblk && ok; ++n) {
+      const int j = kb + n;
+      if (!mbar_wait(st_full, n & 1, kErrTimeoutEpilogue, a.err)) { ok = false; break; }
+      tc_fence_after();
+      // P^T / dS^T tiles are free once the previous block's MMAs finished.
+      if (n > 0 && !mbar_wait(qd_empty, (n - 1) & 1, kErrTimeoutEpilogue, a.err)) { ok = false; break; }
+      const bool diag = n == 0;
+#pragma unroll 1
+      for (int c = 0; c < BQ / 32; ++c) {
+        float s[32], dp[32];
+        tmem_ld_32x32(tmem + lanes + c * 32, s);
+        tmem_ld_32x32(tmem + lanes + 128 + c * 32, dp);
+        uint32_t pp[16], dd[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float pv[2], dv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int qi = c * 32 + i + e;
+            const bool masked = diag && (j * BQ + qi) < key;
+            pv[e] = masked ? 0.f : exp2f(s[i + e] * a.sl2 - sL[qi]);
+            dv[e] = pv[e] * (dp[i + e] - sD[qi]);
+          }
+          pp[i / 2] = pack_bf16x2(pv[0], pv[1]);
+          dd[i / 2] = pack_bf16x2(dv[0], dv[1]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          *reinterpret_cast<uint4*>(sP + tile_off(r, c * 4 + u)) = make_uint4(pp[4 * u], pp[4 * u + 1], pp[4 * u + 2], pp[4 * u + 3]);
+          *reinterpret_cast<uint4*>(sS + tile_off(r, c * 4 + u)) = make_uint4(dd[4 * u], dd[4 * u + 1], dd[4 * u + 2], dd[4 * u + 3]);
+        }
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    if (ok && mbar_wait(kv_done, 0, kErrTimeoutEpilogue, a.err)) {
+      tc_fence_after();
+      if (key < a.T) {
+        __nv_bfloat16* dk = a.dqkv + (long(b) * a.T + key) * 3 * a.C + a.C + h * HD;
+        __nv_bfloat16* dv = dk + a.C;
+#pragma unroll 1
+        for (int c = 0; c < HD / 32; ++c) {
+          float x[32], y[32];
+          tmem_ld_32x32(tmem + lanes + 256 + c * 32, x);
+          tmem_ld_32x32(tmem + lanes + 384 + c * 32, y);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            *reinterpret_cast<uint4*>(dk + c * 32 + u * 8) = make_uint4(
+                pack_bf16x2(x[8 * u] * a.scale, x[8 * u + 1] * a.scale), pack_bf16x2(x[8 * u + 2] * a.scale, x[8 * u + 3] * a.scale),
+                pack_bf16x2(x[8 * u + 4] * a.scale, x[8 * u + 5] * a.scale), pack_bf16x2(x[8 * u + 6] * a.scale, x[8 * u + 7] * a.scale));
+            *reinterpret_cast<uint4*>(dv + c * 32 + u * 8) = make_uint4(
+                pack_bf16x2(y[8 * u], y[8 * u + 1]), pack_bf16x2(y[8 * u + 2], y[8 * u + 3]),
+                pack_bf16x2(y[8 * u + 4], y[8 * u + 5]), pack_bf16x2(y[8 * u + 6], y[8 * u + 7]));
+          }
+        }
+      } else {
+        // Lanes past the sequence still take part in the warp-collective loads.
+#pragma unroll 1
+        for (int c = 0; c < HD / 32; ++c) {
+          float x[32];
+          tmem_ld_32x32(tmem + lanes + 256 + c * 32, x);
+          tmem_ld_32x32(tmem + lanes + 384 + c * 32, x);
+        }
+      }
+    }
+  } else {
+    // dQ drain warpgroup: thread = query row of the current block.
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lanes = uint32_t(quarter * 32) << 16;
+    for (int n = 0; n < nblk; ++n) {
+      const int j = kb + n;
+      if (!mbar_wait(dq_full, n & 1, kErrTimeoutEpilogue, a.err)) break;
+      tc_fence_after();
+      float* dst = a.dq_acc + (long(b) * a.T + j * BQ + r) * a.C + h * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
+        float x[32];
+        tmem_ld_32x32(tmem + lanes + 128 + c * 32, x);
+#pragma unroll
+        for (int u = 0; u < 32; u += 4)
+          atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + u),
+                    make_float4(x[u] * a.scale, x[u + 1] * a.scale, x[u + 2] * a.scale, x[u + 3] * a.scale));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// dQ accumulator (fp32, (B*T, C)) -> bf16 q columns of dqkv.
+__global__ void dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dqkv, long rows, int C) {
+  const long n4 = rows * C / 4;
+  for (long i = long(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += long(gridDim.x) * blockDim.x) {
+    const long row = (i * 4) / C, col = (i * 4) % C;
+    const float4 f = reinterpret_cast<const float4*>(acc)[i];
+    *reinterpret_cast<uint2*>(dqkv + row * 3 * C + col) = make_uint2(pack_bf16x2(f.x, f.y), pack_bf16x2(f.z, f.w));
+  }
+}
+
+bool flash_bwd_tc_supported(int64_t T, int64_t HD) { return HD == 128 && T % 128 == 0; }
+
+// 3-D map over a (B*T, width) bf16 activation: inner `width` columns, then the
+// T rows of one sequence, then B sequences (rows past a sequence read as zeros).
+static CUtensorMap seq_map_3d(void* base, int64_t B, int64_t T, int64_t width) {
+  CUtensorMap m;
+  cuuint64_t dims[3] = {cuuint64_t(width), cuuint64_t(T), cuuint64_t(B)};
+  cuuint64_t strides[2] = {cuuint64_t(width * 2), cuuint64_t(T * width * 2)};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_tiled_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "flash_bwd_tc: tensor map encode failed ", int(r));
+  return m;
+}
+
+void flash_dsum(torch::Tensor out, torch::Tensor dout, torch::Tensor dsum, int64_t B, int64_t T, int64_t H);
+
+// Full backward with the tcgen05 kernel: D precompute, zeroed fp32 dQ
+// accumulator (caller's scratch), the main kernel, then dQ -> bf16.
+void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch::Tensor lse, torch::Tensor dsum,
+                  torch::Tensor dq_acc, torch::Tensor dqkv, int64_t B, int64_t T, int64_t H) {
+  using namespace fb;
+  const int64_t C = qkv.size(1) / 3;
+  TORCH_CHECK(qkv.is_contiguous() && dqkv.is_contiguous() && dout.is_contiguous() && out.is_contiguous(),
+              "flash_bwd_tc: contiguous tensors");
+  TORCH_CHECK(C == H * HD && qkv.size(0) == B * T && flash_bwd_tc_supported(T, C / H), "flash_bwd_tc: shape");
+  TORCH_CHECK(dqkv.sizes() == qkv.sizes() && dout.size(1) == C && out.size(1) == C, "flash_bwd_tc: shapes");
+  TORCH_CHECK(dq_acc.scalar_type() == at::kFloat && dq_acc.numel() == B * T * C && dq_acc.is_contiguous(),
+              "flash_bwd_tc: dq_acc");
+  TORCH_CHECK(lse.numel() == B * H * T && dsum.numel() == B * H * T, "flash_bwd_tc: lse/dsum");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(lse.data_ptr()) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(dsum.data_ptr()) % 16 == 0, "flash_bwd_tc: 16-byte aligned lse/dsum");
+  const at::cuda::CUDAGuard guard(qkv.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  flash_dsum(out, dout, dsum, B, T, H);
+  TORCH_CHECK(cudaMemsetAsync(dq_acc.data_ptr(), 0, size_t(B * T * C) * 4, stream) == cudaSuccess,
+              "flash_bwd_tc: memset");
+  CUtensorMap tm = seq_map_3d(qkv.data_ptr(), B, T, 3 * C);
+  CUtensorMap tmo = seq_map_3d(dout.data_ptr(), B, T, C);
+  FbArgs a{};
+  a.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
+  a.dq_acc = dq_acc.data_ptr<float>();
+  a.lse = lse.data_ptr<float>();
+  a.dsum = dsum.data_ptr<float>();
+  a.B = int(B); a.H = int(H); a.T = int(T); a.C = int(C);
+  a.scale = 1.f / std::sqrt(float(HD));
+  a.sl2 = a.scale * 1.4426950408889634f;
+  a.err = error_word();
+  static bool configured = false;
+  if (!configured) {
+    TORCH_CHECK(cudaFuncSetAttribute(flash_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) ==
+                    cudaSuccess, "flash_bwd_tc: smem");
+    configured = true;
+  }
+  dim3 grid(unsigned(T / BK), unsigned(B * H));
+  flash_bwd_tc_kernel<<<grid, kThreads, kSmem, stream>>>(tm, tmo, a);
+  TORCH_CHECK(cudaGetLastError() == cudaSuccess, "flash_bwd_tc launch failed");
+  dq_convert_kernel<<<148 * 8, 256, 0, stream>>>(a.dq_acc, a.dqkv, B * T, int(C));
+  TORCH_CHECK(cudaGetLastError() == cudaSuccess, "dq_convert launch failed");
+}
+
+}  // namespace nk

@@ -71,6 +71,7 @@ class _Workspace:
             self.dy = torch.empty(m, c, **bf)
             self.dqkv = torch.empty(m, 3 * c, **bf)
             self.dsum = torch.empty(batch * cfg.n_head * seq, **f32)
+            self.dq_acc = torch.empty(m, c, **f32)  # fp32 dQ accumulation of the tcgen05 backward
 
 
 class FusedGpt:
@@ -171,7 +172,8 @@ class FusedGpt:
             # Attention: x' = x + attn(rms(x)) Wproj^T
             gemm.linear_wgrad(dx, ws.y[i], st.grad_of(p + "attn.c_proj.weight"))
             gemm.linear_dgrad(dx, self._w(p + "attn.c_proj.weight"), out=ws.dy)
-            L.flash_attention_bwd(ws.qkv[i], ws.y[i], ws.dy, ws.lse[i], ws.dsum, ws.dqkv, b, t, cfg.n_head)
+            L.flash_attention_bwd(ws.qkv[i], ws.y[i], ws.dy, ws.lse[i], ws.dsum, ws.dqkv, b, t, cfg.n_head,
+                                  dq_acc=ws.dq_acc)
             L.rope_qknorm_bwd(ws.qkv[i], ws.dqkv, ws.rstd_qk[i], self.cos, self.sin, t, cfg.n_head)
             gemm.linear_wgrad(ws.dqkv, ws.h1[i], st.qkv_grad(i))
             gemm.linear_dgrad(ws.dqkv, st.qkv_work(i), out=ws.dh)

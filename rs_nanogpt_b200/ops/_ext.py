@@ -11,7 +11,8 @@ as ``bench.py`` can report how many of this package's kernels were launched
 import functools
 
 # Kernels launched per extension call (1 unless listed).
-_LAUNCHES = {"flash_bwd": 3, "kernel_status": 0, "flash_fwd_tc_supported": 0}
+_LAUNCHES = {"flash_bwd": 3, "flash_bwd_tc": 3, "kernel_status": 0, "flash_fwd_tc_supported": 0,
+             "flash_bwd_tc_supported": 0}
 _count = [0]
 
 

@@ -170,3 +170,28 @@ def test_flash_attention_tcgen05_forward(b, t, h):
     lse2 = torch.empty_like(lse)
     L.flash_attention(qkv, out2, lse2, b, t, h, impl="mma")
     _close(lse, lse2, 1e-3)
+
+
+@pytest.mark.parametrize("b,t,h", [(2, 256, 2), (1, 640, 3)])
+def test_flash_attention_tcgen05_backward(b, t, h):
+    """tcgen05 backward vs fp32 autograd of the reference attention."""
+    from rs_nanogpt_b200.models.reference import attention
+    from rs_nanogpt_b200.ops import layers as L
+    torch.manual_seed(12)
+    d, c = 128, h * 128
+    qkv = torch.randn(b * t, 3 * c, device="cuda").bfloat16()
+    out = torch.empty(b * t, c, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(b * h * t, device="cuda")
+    L.flash_attention(qkv, out, lse, b, t, h, impl="mma")
+    z = qkv.float().clone().requires_grad_(True)
+    q = z[:, :c].view(b, t, h, d).transpose(1, 2)
+    k = z[:, c:2 * c].view(b, t, h, d).transpose(1, 2)
+    v = z[:, 2 * c:].view(b, t, h, d).transpose(1, 2)
+    ref = attention(q, k, v, 0).transpose(1, 2).reshape(b * t, c)
+    dout = torch.randn(b * t, c, device="cuda").bfloat16()
+    ref.backward(dout.float())
+    dsum = torch.empty(b * h * t, device="cuda")
+    dq_acc = torch.empty(b * t, c, device="cuda")
+    dqkv = torch.full_like(qkv, float("nan"))
+    L.flash_attention_bwd(qkv, out, dout, lse, dsum, dqkv, b, t, h, dq_acc=dq_acc, impl="tc")
+    _close(dqkv, z.grad, 3e-2)
