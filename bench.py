@@ -165,8 +165,8 @@ def main():
                        "grad_accum": accum, "parallelism": f"dp{n}", "comm_backend": args.backend,
                        "l2": "inputs larger than L2 (GB-scale activations per micro-batch)"},
             "mfu": mfu, "mfu_peak": f"{peak:.0f} TFLOP/s bf16 ({kind})",
-            "clocks": clocks.summary(), "gpu_launches": launches // max(1, args.steps),
-            "gpu_launches_note": "kernels of this package per optimizer step (per rank)",
+            "clocks": clocks.summary(), "gpu_launches": launches, "gpu_launches_per_step": launches // max(1, args.steps),
+            "gpu_launches_note": "kernels of this package launched in the timed region (per rank)",
             "kernel_status": status, "e2e": e2e,
         }
         print(json.dumps(out))

@@ -30,8 +30,12 @@ void ddp_rs_adam_ag(int64_t grads_dev, int64_t works_dev, int64_t world, torch::
 void flash_fwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor lse, int64_t B, int64_t T, int64_t H);
 bool flash_fwd_tc_supported(int64_t T, int64_t HD);
 void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch::Tensor lse, torch::Tensor dsum,
-                  torch::Tensor dq_acc, torch::Tensor dqkv, int64_t B, int64_t T, int64_t H);
+                  torch::Tensor dq_acc, torch::Tensor dqkv, int64_t B, int64_t T, int64_t H,
+                  c10::optional<torch::Tensor> rope_rstd, c10::optional<torch::Tensor> rope_cos,
+                  c10::optional<torch::Tensor> rope_sin);
 bool flash_bwd_tc_supported(int64_t T, int64_t HD);
+void gemm_qkv_rope(torch::Tensor x, torch::Tensor w, torch::Tensor qkv, torch::Tensor rstd, torch::Tensor cos_t,
+                   torch::Tensor sin_t, int64_t T, int64_t H, double eps);
 }  // namespace nk
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -39,6 +43,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &nk::gemm, "tcgen05 bf16 GEMM with fused epilogues", py::arg("A"), py::arg("a_mn_major"),
         py::arg("B"), py::arg("b_mn_major"), py::arg("C"), py::arg("mode"), py::arg("alpha"), py::arg("aux"),
         py::arg("aux_out"), py::arg("splits"), py::arg("block_n"));
+  m.def("gemm_qkv_rope", &nk::gemm_qkv_rope);
   m.def("kernel_status", &nk::kernel_status, "device error word of the kernels (0 = ok)", py::arg("reset") = true);
   m.def("rmsnorm_fwd", &nk::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &nk::rmsnorm_bwd);

@@ -46,6 +46,13 @@ struct FbArgs {
   int B, H, T, C;
   float scale, sl2;
   int* err;
+  // Optional RoPE + QK-norm backward folded into the dK/dQ write-out:
+  // gradients w.r.t. the pre-RoPE k/q (the forward stored y = rms(rope(x))
+  // in the QKV buffer and 1/denominator per (row, part, head) in rope_rstd).
+  const __nv_bfloat16* qkv;
+  const float* rope_rstd;
+  const float* rope_cos;
+  const float* rope_sin;
 };
 
 __device__ __forceinline__ uint32_t tile_off(int r, int c) {  // 16B chunk c (of 16) in row r, K-major SW128
@@ -219,19 +226,50 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
         __nv_bfloat16* dv = dk + a.C;
 #pragma unroll 1
         for (int c = 0; c < HD / 32; ++c) {
-          float x[32], y[32];
-          tmem_ld_32x32(tmem + lanes + 256 + c * 32, x);
+          float y[32];
           tmem_ld_32x32(tmem + lanes + 384 + c * 32, y);
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            *reinterpret_cast<uint4*>(dk + c * 32 + u * 8) = make_uint4(
-                pack_bf16x2(x[8 * u] * a.scale, x[8 * u + 1] * a.scale), pack_bf16x2(x[8 * u + 2] * a.scale, x[8 * u + 3] * a.scale),
-                pack_bf16x2(x[8 * u + 4] * a.scale, x[8 * u + 5] * a.scale), pack_bf16x2(x[8 * u + 6] * a.scale, x[8 * u + 7] * a.scale));
+          for (int u = 0; u < 4; ++u)
             *reinterpret_cast<uint4*>(dv + c * 32 + u * 8) = make_uint4(
                 pack_bf16x2(y[8 * u], y[8 * u + 1]), pack_bf16x2(y[8 * u + 2], y[8 * u + 3]),
                 pack_bf16x2(y[8 * u + 4], y[8 * u + 5]), pack_bf16x2(y[8 * u + 6], y[8 * u + 7]));
+        }
+        float g[HD];
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+          float x[32];
+          tmem_ld_32x32(tmem + lanes + 256 + c * 32, x);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) g[c * 32 + i] = x[i] * a.scale;
+        }
+        if (a.rope_rstd) {
+          // d/dx of y = rms(rope(x)): dr = r (g - y <g, y> / D), then the transposed rotation.
+          const long row = long(b) * a.T + key;
+          const __nv_bfloat16* yk = a.qkv + row * 3 * a.C + a.C + h * HD;
+          const float r = a.rope_rstd[row * 2 * a.H + a.H + h];
+          float dot = 0.f;
+#pragma unroll
+          for (int i = 0; i < HD; i += 2) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(yk + i));
+            dot += f.x * g[i] + f.y * g[i + 1];
+          }
+          dot /= float(HD);
+          const float* cr = a.rope_cos + long(key) * 64;
+          const float* sr = a.rope_sin + long(key) * 64;
+#pragma unroll
+          for (int i = 0; i < 64; ++i) {
+            const float y1 = __bfloat162float(yk[i]), y2 = __bfloat162float(yk[i + 64]);
+            const float d1 = r * (g[i] - y1 * dot), d2 = r * (g[i + 64] - y2 * dot);
+            const float cs = __ldg(cr + i), sn = __ldg(sr + i);
+            g[i] = d1 * cs - d2 * sn;       // dx1 = dy1 cos - dy2 sin
+            g[i + 64] = d1 * sn + d2 * cs;  // dx2 = dy1 sin + dy2 cos
           }
         }
+#pragma unroll
+        for (int u = 0; u < HD / 8; ++u)
+          *reinterpret_cast<uint4*>(dk + u * 8) =
+              make_uint4(pack_bf16x2(g[8 * u], g[8 * u + 1]), pack_bf16x2(g[8 * u + 2], g[8 * u + 3]),
+                         pack_bf16x2(g[8 * u + 4], g[8 * u + 5]), pack_bf16x2(g[8 * u + 6], g[8 * u + 7]));
       } else {
         // Lanes past the sequence still take part in the warp-collective loads.
 #pragma unroll 1
@@ -274,14 +312,43 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
   }
 }
 
-// dQ accumulator (fp32, (B*T, C)) -> bf16 q columns of dqkv.
-__global__ void dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dqkv, long rows, int C) {
-  const long n4 = rows * C / 4;
-  for (long i = long(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += long(gridDim.x) * blockDim.x) {
-    const long row = (i * 4) / C, col = (i * 4) % C;
-    const float4 f = reinterpret_cast<const float4*>(acc)[i];
-    *reinterpret_cast<uint2*>(dqkv + row * 3 * C + col) = make_uint2(pack_bf16x2(f.x, f.y), pack_bf16x2(f.z, f.w));
+// dQ accumulator (fp32, (B*T, C)) -> bf16 q columns of dqkv, optionally
+// through the RoPE + QK-norm backward. One warp per (token, head); lane l
+// owns elements [4l, 4l+4), its rotation partners live in lane l ^ 16.
+__global__ void dq_finish_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dqkv, long rows, int T,
+                                 int H, int C, const __nv_bfloat16* __restrict__ qkv, const float* __restrict__ rstd,
+                                 const float* __restrict__ cos_t, const float* __restrict__ sin_t) {
+  const long item = long(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (item >= rows * H) return;
+  const long row = item / H;
+  const int h = int(item % H);
+  const float4 g4 = *reinterpret_cast<const float4*>(acc + row * C + h * 128 + lane * 4);
+  float g[4] = {g4.x, g4.y, g4.z, g4.w};
+  if (rstd) {
+    const uint2 w = *reinterpret_cast<const uint2*>(qkv + row * 3 * C + h * 128 + lane * 4);
+    const float2 y0 = unpack_bf16x2(w.x), y1 = unpack_bf16x2(w.y);
+    const float y[4] = {y0.x, y0.y, y1.x, y1.y};
+    float dot = y[0] * g[0] + y[1] * g[1] + y[2] * g[2] + y[3] * g[3];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    dot /= 128.f;
+    const float r = rstd[row * 2 * H + h];
+    const int pos = int(row % T);
+    float dr[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dr[j] = r * (g[j] - y[j] * dot);
+    const bool first = lane < 16;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float partner = __shfl_xor_sync(0xffffffffu, dr[j], 16);
+      const int i = (lane & 15) * 4 + j;
+      const float cs = cos_t[pos * 64 + i], sn = sin_t[pos * 64 + i];
+      g[j] = first ? dr[j] * cs - partner * sn : partner * sn + dr[j] * cs;
+    }
   }
+  *reinterpret_cast<uint2*>(dqkv + row * 3 * C + h * 128 + lane * 4) =
+      make_uint2(pack_bf16x2(g[0], g[1]), pack_bf16x2(g[2], g[3]));
 }
 
 bool flash_bwd_tc_supported(int64_t T, int64_t HD) { return HD == 128 && T % 128 == 0; }
@@ -306,7 +373,9 @@ void flash_dsum(torch::Tensor out, torch::Tensor dout, torch::Tensor dsum, int64
 // Full backward with the tcgen05 kernel: D precompute, zeroed fp32 dQ
 // accumulator (caller's scratch), the main kernel, then dQ -> bf16.
 void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch::Tensor lse, torch::Tensor dsum,
-                  torch::Tensor dq_acc, torch::Tensor dqkv, int64_t B, int64_t T, int64_t H) {
+                  torch::Tensor dq_acc, torch::Tensor dqkv, int64_t B, int64_t T, int64_t H,
+                  c10::optional<torch::Tensor> rope_rstd, c10::optional<torch::Tensor> rope_cos,
+                  c10::optional<torch::Tensor> rope_sin) {
   using namespace fb;
   const int64_t C = qkv.size(1) / 3;
   TORCH_CHECK(qkv.is_contiguous() && dqkv.is_contiguous() && dout.is_contiguous() && out.is_contiguous(),
@@ -334,6 +403,14 @@ void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torc
   a.scale = 1.f / std::sqrt(float(HD));
   a.sl2 = a.scale * 1.4426950408889634f;
   a.err = error_word();
+  if (rope_rstd.has_value()) {
+    TORCH_CHECK(rope_cos.has_value() && rope_sin.has_value() && rope_cos->size(1) == 64 && rope_cos->size(0) >= T,
+                "flash_bwd_tc: rope tables");
+    a.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
+    a.rope_rstd = rope_rstd->data_ptr<float>();
+    a.rope_cos = rope_cos->data_ptr<float>();
+    a.rope_sin = rope_sin->data_ptr<float>();
+  }
   static bool configured = false;
   if (!configured) {
     TORCH_CHECK(cudaFuncSetAttribute(flash_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) ==
@@ -343,8 +420,10 @@ void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torc
   dim3 grid(unsigned(T / BK), unsigned(B * H));
   flash_bwd_tc_kernel<<<grid, kThreads, kSmem, stream>>>(tm, tmo, a);
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "flash_bwd_tc launch failed");
-  dq_convert_kernel<<<148 * 8, 256, 0, stream>>>(a.dq_acc, a.dqkv, B * T, int(C));
-  TORCH_CHECK(cudaGetLastError() == cudaSuccess, "dq_convert launch failed");
+  const long items = B * T * H;
+  dq_finish_kernel<<<unsigned((items + 7) / 8), 256, 0, stream>>>(a.dq_acc, a.dqkv, B * T, int(T), int(H), int(C),
+                                                                a.qkv, a.rope_rstd, a.rope_cos, a.rope_sin);
+  TORCH_CHECK(cudaGetLastError() == cudaSuccess, "dq_finish launch failed");
 }
 
 }  // namespace nk

@@ -33,6 +33,7 @@ enum GemmMode : int {
   kDRelu2 = 2,      // C = alpha*acc * 2*relu(AUX)
   kResidual = 3,    // C = alpha*acc + AUX (AUX may alias C)
   kAtomicF32 = 4,   // C(fp32) += alpha*acc   (split-K capable)
+  kRopeNorm = 5,    // QKV projection: q and k heads get RoPE + RMSNorm over head_dim, v stored plain
 };
 
 struct GemmArgs {
@@ -48,6 +49,14 @@ struct GemmArgs {
   __nv_bfloat16* aux_out;
   long ld_aux_out;
   int* err;
+  // kRopeNorm: half-split RoPE at position (row % rope_T), then RMSNorm over
+  // each 128-wide head, on columns [0, 2 * rope_C); 1/denominator per
+  // (row, part, head) goes to rope_rstd[row * 2H + part * H + head].
+  const float* rope_cos;
+  const float* rope_sin;
+  float* rope_rstd;
+  int rope_T, rope_H, rope_C;
+  float rope_eps;
 };
 
 constexpr int BM = 128, BK = 64, kGroupM = 16;
@@ -239,6 +248,54 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&acc_full[b], acc_phase, kErrTimeoutEpilogue, args.err)) break;
       tc_fence_after();
       const int row0 = m * BM + q * 32;
+      if (args.mode == kRopeNorm && n * BN + half * 128 < 2 * args.rope_C) {
+        // One full q/k head per thread row: 4 TMEM chunks -> RoPE -> RMSNorm -> 4 TMA stores.
+        const int colb = n * BN + half * 128;
+        const int part = colb / args.rope_C, head = (colb % args.rope_C) / 128;
+        const int row = row0 + lane;
+        const int pos = (row < args.M ? row : 0) % args.rope_T;
+        float hv[128];
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          float v[32];
+          tmem_ld_32x32(tmem_base + (uint32_t(q * 32) << 16) + b * BN + (half * 4 + c4) * 32, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) hv[c4 * 32 + i] = __bfloat162float(__float2bfloat16(args.alpha * v[i]));
+        }
+        const float* cr = args.rope_cos + long(pos) * 64;
+        const float* sr = args.rope_sin + long(pos) * 64;
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const float cs = __ldg(cr + i), sn = __ldg(sr + i);
+          const float x1 = hv[i], x2 = hv[i + 64];
+          hv[i] = x1 * cs + x2 * sn;       // y1 = x1 cos + x2 sin
+          hv[i + 64] = x2 * cs - x1 * sn;  // y2 = x2 cos - x1 sin
+          ss += hv[i] * hv[i] + hv[i + 64] * hv[i + 64];
+        }
+        const float denom = __bfloat162float(__float2bfloat16(sqrtf(ss / 128.f + args.rope_eps)));
+        const float inv = 1.f / denom;
+        if (row < args.M) args.rope_rstd[long(row) * 2 * args.rope_H + part * args.rope_H + head] = inv;
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          float x[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) x[i] = hv[c4 * 32 + i] / denom;
+          if (lane == 0) bulk_wait_read<0>();
+          __syncwarp();
+          stage_row_store(buf_o, lane, x);
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, buf_o, colb + c4 * 32, row0);
+            bulk_commit();
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[b]);
+        continue;
+      }
 #pragma unroll 1
       for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
         const int col0 = n * BN + c * 32;
@@ -340,9 +397,9 @@ static void check_bf16_2d(const torch::Tensor& t, int64_t rows, int64_t cols, co
 
 // C (op)= alpha * A . B^T with operand layouts:
 //   A: a_mn_major ? [K, M] : [M, K]      B: b_mn_major ? [K, N] : [N, K]
-void gemm(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_major, torch::Tensor C, int64_t mode,
-          double alpha, c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> aux_out, int64_t splits,
-          int64_t block_n) {
+void gemm_impl(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_major, torch::Tensor C, int64_t mode,
+               double alpha, c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> aux_out, int64_t splits,
+               int64_t block_n, const GemmArgs* rope) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda(), "gemm: CUDA tensors required");
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm: bf16 operands");
   TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "gemm: 2-D tensors");
@@ -368,6 +425,10 @@ void gemm(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_major, to
   args.C = C.data_ptr();
   args.ldc = C.stride(0);
   args.err = error_word();
+  if (rope) {
+    args.rope_cos = rope->rope_cos; args.rope_sin = rope->rope_sin; args.rope_rstd = rope->rope_rstd;
+    args.rope_T = rope->rope_T; args.rope_H = rope->rope_H; args.rope_C = rope->rope_C; args.rope_eps = rope->rope_eps;
+  }
   if (mode == kDRelu2 || mode == kResidual) {
     TORCH_CHECK(aux.has_value(), "gemm: mode needs aux");
     check_bf16_2d(*aux, M, N, "aux");
@@ -407,6 +468,30 @@ void gemm(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_major, to
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   if (BN == 128) launch<128>(args, ta, tb, tc, tx, stream);
   else launch<256>(args, ta, tb, tc, tx, stream);
+}
+
+void gemm(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_major, torch::Tensor C, int64_t mode,
+          double alpha, c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> aux_out, int64_t splits,
+          int64_t block_n) {
+  TORCH_CHECK(mode != kRopeNorm, "gemm: use gemm_qkv_rope for the RoPE epilogue");
+  gemm_impl(A, a_mn_major, B, b_mn_major, C, mode, alpha, aux, aux_out, splits, block_n, nullptr);
+}
+
+// qkv[M, 3C] = x[M, C] . w[3C, C]^T with RoPE + QK-RMSNorm fused into the
+// epilogue for the q and k column blocks (head_dim 128, 3C % 256 == 0).
+void gemm_qkv_rope(torch::Tensor x, torch::Tensor w, torch::Tensor qkv, torch::Tensor rstd, torch::Tensor cos_t,
+                   torch::Tensor sin_t, int64_t T, int64_t H, double eps) {
+  const int64_t C = w.size(1);
+  TORCH_CHECK(w.size(0) == 3 * C && C == H * 128 && (3 * C) % 256 == 0, "gemm_qkv_rope: shape");
+  TORCH_CHECK(cos_t.scalar_type() == at::kFloat && cos_t.is_contiguous() && cos_t.size(1) == 64 &&
+                  sin_t.is_contiguous() && cos_t.size(0) >= T, "gemm_qkv_rope: rope tables");
+  TORCH_CHECK(rstd.scalar_type() == at::kFloat && rstd.numel() >= x.size(0) * 2 * H, "gemm_qkv_rope: rstd");
+  GemmArgs r{};
+  r.rope_cos = cos_t.data_ptr<float>();
+  r.rope_sin = sin_t.data_ptr<float>();
+  r.rope_rstd = rstd.data_ptr<float>();
+  r.rope_T = int(T); r.rope_H = int(H); r.rope_C = int(C); r.rope_eps = float(eps);
+  gemm_impl(x, false, w, false, qkv, kRopeNorm, 1.0, c10::nullopt, c10::nullopt, 1, 256, &r);
 }
 
 }  // namespace nk

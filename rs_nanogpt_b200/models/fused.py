@@ -84,6 +84,9 @@ class FusedGpt:
         cos, sin = rope_tables(self.cfg, store.device)
         self.cos, self.sin = cos.contiguous(), sin.contiguous()
         self._ws: Dict[Tuple[int, int, bool], _Workspace] = {}
+        # RoPE + QK-norm live in the QKV GEMM epilogue (forward) and in the
+        # attention backward's dQ/dK write-out when the shapes allow it.
+        self.fuse_rope = gemm.qkv_rope_supported(self.cfg.n_embd, self.cfg.head_dim)
 
     def workspace(self, batch: int, seq: int, train: bool) -> _Workspace:
         key = (batch, seq, train)
@@ -103,8 +106,12 @@ class FusedGpt:
             j = i if train else 0
             p = f"blocks.{i}."
             h1 = L.rmsnorm(x, eps, out=ws.h1[j], rstd=ws.rstd1[j])
-            qkv = gemm.linear(h1, st.qkv_work(i), out=ws.qkv[j])
-            L.rope_qknorm(qkv, ws.rstd_qk[j], self.cos, self.sin, t, cfg.n_head, eps)
+            if self.fuse_rope:
+                qkv = gemm.linear_qkv_rope(h1, st.qkv_work(i), ws.qkv[j], ws.rstd_qk[j], self.cos, self.sin, t,
+                                           cfg.n_head, eps)
+            else:
+                qkv = gemm.linear(h1, st.qkv_work(i), out=ws.qkv[j])
+                L.rope_qknorm(qkv, ws.rstd_qk[j], self.cos, self.sin, t, cfg.n_head, eps)
             L.flash_attention(qkv, ws.y[j], ws.lse[j], b, t, cfg.n_head)
             xmid = gemm.linear_residual(ws.y[j], self._w(p + "attn.c_proj.weight"), x, out=ws.xmid[j])
             h2 = L.rmsnorm(xmid, eps, out=ws.h2[j], rstd=ws.rstd2[j])
@@ -172,9 +179,10 @@ class FusedGpt:
             # Attention: x' = x + attn(rms(x)) Wproj^T
             gemm.linear_wgrad(dx, ws.y[i], st.grad_of(p + "attn.c_proj.weight"))
             gemm.linear_dgrad(dx, self._w(p + "attn.c_proj.weight"), out=ws.dy)
-            L.flash_attention_bwd(ws.qkv[i], ws.y[i], ws.dy, ws.lse[i], ws.dsum, ws.dqkv, b, t, cfg.n_head,
-                                  dq_acc=ws.dq_acc)
-            L.rope_qknorm_bwd(ws.qkv[i], ws.dqkv, ws.rstd_qk[i], self.cos, self.sin, t, cfg.n_head)
+            folded = L.flash_attention_bwd(ws.qkv[i], ws.y[i], ws.dy, ws.lse[i], ws.dsum, ws.dqkv, b, t, cfg.n_head,
+                                           dq_acc=ws.dq_acc, rope=(ws.rstd_qk[i], self.cos, self.sin))
+            if not folded:
+                L.rope_qknorm_bwd(ws.qkv[i], ws.dqkv, ws.rstd_qk[i], self.cos, self.sin, t, cfg.n_head)
             gemm.linear_wgrad(ws.dqkv, ws.h1[i], st.qkv_grad(i))
             gemm.linear_dgrad(ws.dqkv, st.qkv_work(i), out=ws.dh)
             L.rmsnorm_bwd(ws.x[i], ws.dh, ws.rstd1[i], dx=dx, accumulate=True)

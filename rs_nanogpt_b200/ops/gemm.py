@@ -54,6 +54,18 @@ def linear_residual(x, w, residual, out=None):
     return out
 
 
+def qkv_rope_supported(n_embd: int, head_dim: int) -> bool:
+    return head_dim == 128 and (3 * n_embd) % 256 == 0
+
+
+def linear_qkv_rope(x, w_qkv, out, rstd, cos, sin, seq_len: int, n_head: int, eps: float):
+    """out = x w_qkv^T with RoPE (positions row % seq_len) and RMSNorm over each
+    q/k head fused into the GEMM epilogue; 1/denominator per (row, q|k, head)
+    goes to rstd (the layout the RoPE backward reads)."""
+    ext().gemm_qkv_rope(x, w_qkv, out, rstd, cos, sin, seq_len, n_head, eps)
+    return out
+
+
 def linear_dgrad(dy, w, out=None, alpha: float = 1.0):
     """dx[M,K] = alpha * dy[M,N] @ w[N,K]."""
     if out is None:

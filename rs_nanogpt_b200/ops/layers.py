@@ -71,13 +71,17 @@ def flash_attention(qkv, out, lse, batch: int, seq_len: int, n_head: int, impl: 
 
 
 def flash_attention_bwd(qkv, out, dout, lse, dsum, dqkv, batch: int, seq_len: int, n_head: int,
-                        dq_acc=None, impl: str = "auto") -> None:
+                        dq_acc=None, impl: str = "auto", rope=None) -> bool:
     """Causal attention backward into dqkv (dQ | dK | dV). The tcgen05 kernel
     (head_dim 128, seq_len % 128 == 0) needs ``dq_acc``, an fp32 (tokens, C)
-    scratch buffer for the dQ accumulation; without it the mma.sync kernels run."""
+    scratch buffer for the dQ accumulation; without it the mma.sync kernels run.
+    ``rope=(rstd, cos, sin)`` folds the RoPE + QK-norm backward into the dQ/dK
+    write-out (tcgen05 path only). Returns True when that fold happened."""
     hd = qkv.shape[1] // 3 // n_head
     use_tc = impl == "tc" or (impl == "auto" and dq_acc is not None and ext().flash_bwd_tc_supported(seq_len, hd))
     if use_tc:
-        ext().flash_bwd_tc(qkv, out, dout, lse, dsum, dq_acc, dqkv, batch, seq_len, n_head)
-    else:
-        ext().flash_bwd(qkv, out, dout, lse, dsum, dqkv, batch, seq_len, n_head)
+        r = rope if rope is not None else (None, None, None)
+        ext().flash_bwd_tc(qkv, out, dout, lse, dsum, dq_acc, dqkv, batch, seq_len, n_head, *r)
+        return rope is not None
+    ext().flash_bwd(qkv, out, dout, lse, dsum, dqkv, batch, seq_len, n_head)
+    return False

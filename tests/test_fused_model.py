@@ -9,14 +9,14 @@ def _rel(a, b):
     return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
 
 
-@pytest.mark.parametrize("mode", ["reference", "bench"])
-def test_fused_forward_backward_matches_reference(mode):
+@pytest.mark.parametrize("mode,seq", [("reference", 128), ("bench", 128), ("bench", 256)])
+def test_fused_forward_backward_matches_reference(mode, seq):
     from rs_nanogpt_b200.config import GptConfig
     from rs_nanogpt_b200.models.fused import FusedGpt
     from rs_nanogpt_b200.models.params import ParamStore, init_params
     from rs_nanogpt_b200.models.reference import ReferenceGpt, cross_entropy_sum_count
 
-    cfg = GptConfig(vocab_size=1024, sequence_len=128, n_layer=2, n_head=2, n_embd=256, rope_base=10000.0)
+    cfg = GptConfig(vocab_size=1024, sequence_len=seq, n_layer=2, n_head=2, n_embd=256, rope_base=10000.0)
     store = ParamStore(cfg, "cuda")
     init_params(store, seed=0, mode=mode)
     # Non-zero output projections so every path carries gradient.
@@ -25,7 +25,7 @@ def test_fused_forward_backward_matches_reference(mode):
         if n.endswith("c_proj.weight"):
             store.param(n).normal_(0, 0.02, generator=g)
     store.refresh_work()
-    b, t = 2, 128
+    b, t = 2, seq
     idx = torch.randint(0, cfg.vocab_size, (b, t), device="cuda")
     tgt = torch.randint(0, cfg.vocab_size, (b, t), device="cuda")
     tgt[0, :7] = -1
@@ -51,3 +51,23 @@ def test_fused_forward_backward_matches_reference(mode):
         a = fused_grad[sl.offset:sl.offset + sl.numel]
         r = ref_grad[sl.offset:sl.offset + sl.numel]
         assert _rel(a, r) < 6e-2, f"{name}: rel err {_rel(a, r)}"
+
+
+def test_qkv_gemm_with_fused_rope_matches_separate_kernels():
+    from rs_nanogpt_b200.config import GptConfig
+    from rs_nanogpt_b200.models.reference import rope_tables
+    from rs_nanogpt_b200.ops import gemm
+    from rs_nanogpt_b200.ops import layers as L
+    torch.manual_seed(3)
+    cfg = GptConfig(sequence_len=256, n_head=2, n_embd=256, rope_base=10000.0)
+    cos, sin = rope_tables(cfg, "cuda")
+    x = torch.randn(512, 256, device="cuda").bfloat16()
+    w = (torch.randn(768, 256, device="cuda") * 0.05).bfloat16()
+    ref = gemm.linear(x, w)
+    r1 = torch.empty(512 * 4, device="cuda")
+    L.rope_qknorm(ref, r1, cos, sin, 256, 2, 1e-6)
+    out = torch.empty_like(ref)
+    r2 = torch.empty_like(r1)
+    gemm.linear_qkv_rope(x, w, out, r2, cos, sin, 256, 2, 1e-6)
+    assert (out.float() - ref.float()).abs().max().item() < 3e-2
+    assert (r1 - r2).abs().max().item() < 1e-3 * r1.abs().max().item()
