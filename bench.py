@@ -157,7 +157,7 @@ def main():
         mfu = tok_s / n * cfg.flops_per_token() / (peak * 1e12)
         out = {
             "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": n, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic uniform-random token ids; random-init weights (N(0,0.02), zero-init projections)",
             "config": {"model": f"GPT d{args.depth} (n_embd {cfg.n_embd}, {cfg.n_head} heads x 128, vocab 65536)",

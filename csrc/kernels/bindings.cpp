@@ -36,6 +36,14 @@ void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torc
 bool flash_bwd_tc_supported(int64_t T, int64_t HD);
 void gemm_qkv_rope(torch::Tensor x, torch::Tensor w, torch::Tensor qkv, torch::Tensor rstd, torch::Tensor cos_t,
                    torch::Tensor sin_t, int64_t T, int64_t H, double eps);
+void kv_rope_append(torch::Tensor qkv, torch::Tensor k_cache, torch::Tensor v_cache, c10::optional<torch::Tensor> pos,
+                    c10::optional<torch::Tensor> lens, int64_t rows_per_seq, int64_t H, torch::Tensor cos_t,
+                    torch::Tensor sin_t, bool do_rope, double eps);
+void decode_attention(torch::Tensor qkv, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor pos,
+                      torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml, int64_t chunk);
+void sample_tokens(torch::Tensor logits, double temperature, int64_t top_k, torch::Tensor uniforms,
+                   torch::Tensor gen_count, torch::Tensor out_tokens, torch::Tensor next_in, torch::Tensor pos,
+                   bool advance_pos);
 }  // namespace nk
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -62,4 +70,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_fwd_tc_supported", &nk::flash_fwd_tc_supported);
   m.def("ddp_barrier", &nk::ddp_barrier);
   m.def("ddp_rs_adam_ag", &nk::ddp_rs_adam_ag);
+  m.def("kv_rope_append", &nk::kv_rope_append);
+  m.def("decode_attention", &nk::decode_attention);
+  m.def("sample_tokens", &nk::sample_tokens);
 }

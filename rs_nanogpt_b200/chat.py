@@ -11,7 +11,7 @@ import sys
 
 import torch
 
-from .eval.sample import CachedModel, SampleOptions, generate_ids
+from .eval.sample import SampleOptions, cached_model, generate_ids
 from .tokenizer import BpeTokenizer
 from .utils import checkpoint
 
@@ -82,7 +82,7 @@ def run_chat(args) -> None:
         raise ValueError(f"vocab {args.vocab} has {tok.vocab_size()} tokens but the checkpoint was trained with "
                          f"{meta.config.vocab_size}; a mismatched vocabulary loads fine and scores garbage")
     store, _ = checkpoint.load(args.checkpoint, device)
-    model = CachedModel(store)
+    model = cached_model(store)
     print(f"chat: {args.checkpoint} | step {meta.step} | val_bpb {meta.val_bpb:.4f} | context "
           f"{meta.config.sequence_len} tokens")
     print(f"sampling: temperature {args.temperature} | top_k {args.top_k} | max_tokens {args.max_tokens} | "

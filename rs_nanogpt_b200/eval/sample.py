@@ -109,3 +109,12 @@ class CachedModel:
     def forward_with_cache(self, feed: Sequence[int], cache) -> torch.Tensor:
         x = torch.tensor([list(feed)], dtype=torch.long, device=self.device)
         return self.ref.forward(x, cache)[0, -1]
+
+
+def cached_model(store):
+    """The generation model for ``store``: the fused CUDA decode engine on a
+    GPU (head_dim 128), else the PyTorch-op model."""
+    if store.device.type == "cuda" and store.cfg.head_dim == 128 and store.work is not None:
+        from ..models.decode import FusedCachedModel
+        return FusedCachedModel(store)
+    return CachedModel(store)

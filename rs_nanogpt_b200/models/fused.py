@@ -97,7 +97,9 @@ class FusedGpt:
     def _w(self, name):
         return self.store.work_of(name)
 
-    def _forward_blocks(self, idx: torch.Tensor, ws: _Workspace, train: bool) -> torch.Tensor:
+    def _forward_blocks(self, idx: torch.Tensor, ws: _Workspace, train: bool, kv_hook=None) -> torch.Tensor:
+        """Embedding, blocks and final norm. ``kv_hook(layer, qkv)`` sees each
+        layer's QKV activation after RoPE + QK-norm (the KV-cache prefill)."""
         cfg, st = self.cfg, self.store
         b, t = idx.shape
         eps = cfg.norm_eps
@@ -112,6 +114,8 @@ class FusedGpt:
             else:
                 qkv = gemm.linear(h1, st.qkv_work(i), out=ws.qkv[j])
                 L.rope_qknorm(qkv, ws.rstd_qk[j], self.cos, self.sin, t, cfg.n_head, eps)
+            if kv_hook is not None:
+                kv_hook(i, qkv)
             L.flash_attention(qkv, ws.y[j], ws.lse[j], b, t, cfg.n_head)
             xmid = gemm.linear_residual(ws.y[j], self._w(p + "attn.c_proj.weight"), x, out=ws.xmid[j])
             h2 = L.rmsnorm(xmid, eps, out=ws.h2[j], rstd=ws.rstd2[j])

@@ -10,9 +10,11 @@ as ``bench.py`` can report how many of this package's kernels were launched
 """
 import functools
 
-# Kernels launched per extension call (1 unless listed).
+# Kernels launched per extension call (1 unless listed; a callable gets the
+# call's arguments).
 _LAUNCHES = {"flash_bwd": 3, "flash_bwd_tc": 3, "kernel_status": 0, "flash_fwd_tc_supported": 0,
-             "flash_bwd_tc_supported": 0}
+             "flash_bwd_tc_supported": 0,
+             "decode_attention": lambda qkv, kc, vc, pos, out, po, pm, chunk: 1 + int(kc.shape[2] > chunk)}
 _count = [0]
 
 
@@ -25,7 +27,7 @@ class _Counted:
         n = _LAUNCHES.get(name, 1)
 
         def call(*args, **kwargs):
-            _count[0] += n
+            _count[0] += n(*args, **kwargs) if callable(n) else n
             return fn(*args, **kwargs)
 
         return call

@@ -85,3 +85,28 @@ def flash_attention_bwd(qkv, out, dout, lse, dsum, dqkv, batch: int, seq_len: in
         return rope is not None
     ext().flash_bwd(qkv, out, dout, lse, dsum, dqkv, batch, seq_len, n_head)
     return False
+
+
+# ---- inference (csrc/kernels/decode.cu) -----------------------------------------
+
+def kv_rope_append(qkv, k_cache, v_cache, pos, lens, rows_per_seq: int, n_head: int, cos, sin,
+                   do_rope: bool, eps: float) -> None:
+    """Write the k, v of every row of ``qkv`` (tokens, 3C) into the layer's
+    caches (B, H, capacity, 128) at position ``pos[s] + row % rows_per_seq`` of
+    sequence ``s = row // rows_per_seq`` (``pos`` None = 0), skipping rows at or
+    beyond ``lens[s]``; with ``do_rope`` first apply RoPE + QK-RMSNorm to the
+    row's q and k in place."""
+    ext().kv_rope_append(qkv, k_cache, v_cache, pos, lens, rows_per_seq, n_head, cos, sin, do_rope, eps)
+
+
+def decode_attention(qkv, k_cache, v_cache, pos, out, part_o, part_ml, chunk: int = 128) -> None:
+    """One query row per sequence (row b of ``qkv``) against cached keys
+    0..pos[b]; writes (B, C) bf16. ``part_o``/``part_ml`` are fp32 scratch of
+    at least B*H*ceil(capacity/chunk)*128 and *2 elements."""
+    ext().decode_attention(qkv, k_cache, v_cache, pos, out, part_o, part_ml, chunk)
+
+
+def sample_tokens(logits, temperature: float, top_k: int, uniforms, gen_count, out_tokens, next_in, pos,
+                  advance_pos: bool) -> None:
+    """On-device greedy / top-k sampling of one token per logits row."""
+    ext().sample_tokens(logits, temperature, top_k, uniforms, gen_count, out_tokens, next_in, pos, advance_pos)

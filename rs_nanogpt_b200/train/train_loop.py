@@ -108,7 +108,7 @@ def train(engine: TrainEngine, batches, cfg: TrainConfig, ev: EvalContext, fault
     `batches.next_batch()` yields objects with `.inputs` / `.targets`.
     `fault`, when given, is called as fault(step, micro) before each
     micro-batch (host-side fault injection for tests)."""
-    from ..eval.sample import CachedModel, SampleOptions, generate_ids
+    from ..eval.sample import SampleOptions, cached_model, generate_ids
 
     dist = engine.dist
     store = engine.store
@@ -138,7 +138,7 @@ def train(engine: TrainEngine, batches, cfg: TrainConfig, ev: EvalContext, fault
             opts = SampleOptions(ev.sample_tokens, ev.sample_temperature, 0, step)
             stops = ev.tokenizer.assistant_stop_ids() if ev.sample_chat else []
             prompts = CHAT_SAMPLE_PROMPTS if ev.sample_chat else SAMPLE_PROMPTS
-            model = CachedModel(store)
+            model = cached_model(store)
             for p in prompts:
                 ids = generate_ids(model, sample_prefix(ev.tokenizer, p, ev.sample_chat), opts, stops)
                 print(f"sample {p!r} -> {ev.tokenizer.decode_lossy(ids)!r}", flush=True)

@@ -1,0 +1,196 @@
+"""KV-cache decode kernels and the decode engine vs PyTorch fp32 references."""
+import math
+
+import pytest
+import torch
+
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("kernel_ok")]
+
+
+def _close(out, ref, tol):
+    err = (out.float() - ref.float()).abs().max().item()
+    scale = max(1.0, ref.float().abs().max().item())
+    assert err <= tol * scale, f"max err {err} > {tol * scale}"
+
+
+def _tables(h, seq=256):
+    from rs_nanogpt_b200.config import GptConfig
+    from rs_nanogpt_b200.models.reference import rope_tables
+    cfg = GptConfig(sequence_len=seq, n_head=h, n_embd=h * 128, rope_base=10000.0)
+    cos, sin = rope_tables(cfg, "cuda")
+    return cos.contiguous(), sin.contiguous()
+
+
+def test_kv_rope_append_decode_rows():
+    from rs_nanogpt_b200.models.reference import apply_rope, rms_norm
+    from rs_nanogpt_b200.ops import layers as L
+    torch.manual_seed(0)
+    b, h, cap = 5, 3, 64
+    c = h * 128
+    cos, sin = _tables(h)
+    qkv = torch.randn(b, 3 * c, device="cuda").bfloat16()
+    orig = qkv.clone()
+    pos = torch.tensor([0, 7, 63, 12, 40], device="cuda", dtype=torch.int32)
+    kc = torch.zeros(b, h, cap, 128, device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    L.kv_rope_append(qkv, kc, vc, pos, None, 1, h, cos, sin, True, 1e-6)
+    for i in range(b):
+        p = int(pos[i])
+        for part in range(2):
+            x = orig[i, part * c:(part + 1) * c].float().view(1, h, 1, 128)
+            ref = rms_norm(apply_rope(x, cos, sin, p), 1e-6).view(c)
+            _close(qkv[i, part * c:(part + 1) * c], ref, 2e-2)
+        _close(kc[i, :, p], qkv[i, c:2 * c].view(h, 128), 0)
+        _close(vc[i, :, p], orig[i, 2 * c:].view(h, 128), 0)
+    assert kc.float().abs().sum(dim=(1, 3)).count_nonzero() == b  # one position per sequence
+
+
+def test_kv_append_prefill_rows_respects_lengths():
+    from rs_nanogpt_b200.ops import layers as L
+    torch.manual_seed(1)
+    b, t, h, cap = 3, 16, 2, 32
+    c = h * 128
+    cos, sin = _tables(h)
+    qkv = torch.randn(b * t, 3 * c, device="cuda").bfloat16()
+    lens = torch.tensor([16, 5, 1], device="cuda", dtype=torch.int32)
+    kc = torch.zeros(b, h, cap, 128, device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    L.kv_rope_append(qkv, kc, vc, None, lens, t, h, cos, sin, False, 1e-6)
+    for i in range(b):
+        n = int(lens[i])
+        rows = qkv[i * t:i * t + n]
+        _close(kc[i, :, :n].transpose(0, 1).reshape(n, c), rows[:, c:2 * c], 0)
+        _close(vc[i, :, :n].transpose(0, 1).reshape(n, c), rows[:, 2 * c:], 0)
+        assert kc[i, :, n:].abs().sum().item() == 0
+
+
+@pytest.mark.parametrize("cap,chunk", [(64, 128), (300, 64), (1280, 128)])
+def test_decode_attention(cap, chunk):
+    from rs_nanogpt_b200.ops import layers as L
+    torch.manual_seed(2)
+    b, h = 4, 3
+    c = h * 128
+    qkv = torch.randn(b, 3 * c, device="cuda").bfloat16()
+    kc = torch.randn(b, h, cap, 128, device="cuda").bfloat16()
+    vc = torch.randn(b, h, cap, 128, device="cuda").bfloat16()
+    pos = torch.tensor([0, cap // 3, cap - 1, 5], device="cuda", dtype=torch.int32)
+    splits = (cap + chunk - 1) // chunk
+    po = torch.empty(b * h * splits * 128, device="cuda")
+    pm = torch.empty(b * h * splits * 2, device="cuda")
+    out = torch.empty(b, c, device="cuda", dtype=torch.bfloat16)
+    L.decode_attention(qkv, kc, vc, pos, out, po, pm, chunk)
+    for i in range(b):
+        n = int(pos[i]) + 1
+        q = qkv[i, :c].float().view(h, 1, 128)
+        s = q @ kc[i, :, :n].float().transpose(1, 2) / math.sqrt(128)
+        ref = torch.softmax(s, -1) @ vc[i, :, :n].float()
+        _close(out[i].view(h, 128), ref.view(h, 128), 1e-2)
+
+
+def _ref_draw(row, temperature, top_k, u):
+    """Index-order inverse-CDF draw over the top-k logits (ties at the
+    threshold kept lowest index first), the rule of the sampling kernel."""
+    import numpy as np
+    v = row.double().numpy()
+    n = v.size
+    if temperature <= 0:
+        return int(np.flatnonzero(v == v.max())[-1])
+    keep = np.ones(n, dtype=bool)
+    if 0 < top_k < n:
+        order = np.lexsort((np.arange(n), -v))
+        keep = np.zeros(n, dtype=bool)
+        keep[order[:top_k]] = True
+    w = np.where(keep, np.exp((v - v.max()) / temperature), 0.0)
+    cum = np.cumsum(w)
+    return int(np.flatnonzero(cum > u * cum[-1])[0])
+
+
+@pytest.mark.parametrize("temperature,top_k,v", [(0.0, 0, 1000), (1.0, 50, 65536), (0.7, 0, 4096), (1.0, 3, 500)])
+def test_sample_tokens_matches_reference_rule(temperature, top_k, v):
+    from rs_nanogpt_b200.ops import layers as L
+    torch.manual_seed(3)
+    b, steps = 6, 2
+    logits = (torch.randn(b, v, device="cuda") * 2).bfloat16()
+    logits[0, 10] = logits[0, 20] = logits[0].max() + 1  # a tie at the maximum
+    uniforms = torch.rand(steps, b, dtype=torch.float64, device="cuda")
+    gen = torch.zeros(b, device="cuda", dtype=torch.int32)
+    out = torch.zeros(b, steps, device="cuda", dtype=torch.int32)
+    nxt = torch.zeros(b, device="cuda", dtype=torch.int64)
+    pos = torch.zeros(b, device="cuda", dtype=torch.int32)
+    L.sample_tokens(logits, temperature, top_k, uniforms, gen, out, nxt, pos, True)
+    torch.cuda.synchronize()
+    assert gen.tolist() == [1] * b and pos.tolist() == [1] * b
+    host = logits.float().cpu()
+    for i in range(b):
+        ref = _ref_draw(host[i], temperature, top_k, float(uniforms[0, i]))
+        assert int(out[i, 0]) == ref == int(nxt[i]), (i, int(out[i, 0]), ref)
+
+
+def _engine_setup(depth=2, seq=512, vocab=1000):
+    from rs_nanogpt_b200.config import d_model
+    from rs_nanogpt_b200.models.params import ParamStore, init_params
+    cfg = d_model(depth, vocab_size=vocab, sequence_len=seq)
+    store = ParamStore(cfg, "cuda")
+    init_params(store, seed=5, mode="bench")
+    store.refresh_work()
+    return cfg, store
+
+
+def test_decode_engine_prefill_and_steps_match_oracle():
+    from rs_nanogpt_b200.models.decode import DecodeEngine
+    from rs_nanogpt_b200.models.reference import ReferenceGpt
+    torch.manual_seed(4)
+    cfg, store = _engine_setup()
+    ref = ReferenceGpt(store, torch.float32)
+    lens = [37, 256, 100]
+    b, tpad = len(lens), 256
+    prompts = [torch.randint(0, cfg.vocab_size, (n,)) for n in lens]
+    ids = torch.zeros(b, tpad, dtype=torch.int64)
+    for i, p in enumerate(prompts):
+        ids[i, :len(p)] = p
+    eng = DecodeEngine(store, b, 320)
+    logits = eng.prefill(ids.cuda(), torch.tensor(lens, dtype=torch.int32).cuda())
+    for i, p in enumerate(prompts):
+        r = ref.forward(p.view(1, -1).cuda())[0, -1]
+        _close(logits[i], r, 5e-2)
+    seqs = [p.tolist() for p in prompts]
+    for _ in range(3):
+        nxt = torch.randint(0, cfg.vocab_size, (b,))
+        eng.next_in.copy_(nxt.cuda())
+        logits = eng.step()
+        eng.pos.add_(1)
+        for i in range(b):
+            seqs[i].append(int(nxt[i]))
+            r = ref.forward(torch.tensor([seqs[i]]).cuda())[0, -1]
+            _close(logits[i], r, 5e-2)
+
+
+def test_generate_batch_graph_equals_eager():
+    from rs_nanogpt_b200.models.decode import DecodeEngine, generate_batch
+    torch.manual_seed(6)
+    cfg, store = _engine_setup()
+    prompts = [torch.randint(0, cfg.vocab_size, (n,)).tolist() for n in (10, 200, 64, 129)]
+    eng = DecodeEngine(store, len(prompts), 256 + 16)
+    a = generate_batch(eng, prompts, 16, 1.0, 50, seed=0, use_graph=False)
+    eng2 = DecodeEngine(store, len(prompts), 256 + 16)
+    bb = generate_batch(eng2, prompts, 16, 1.0, 50, seed=0, use_graph=True)
+    assert a == bb
+    assert all(len(r) == 16 and all(0 <= t < cfg.vocab_size for t in r) for r in a)
+
+
+def test_fused_cached_model_greedy_generation():
+    from rs_nanogpt_b200.eval.sample import SampleOptions, cached_model, generate_ids
+    from rs_nanogpt_b200.models.decode import FusedCachedModel
+    from rs_nanogpt_b200.models.reference import ReferenceGpt
+    cfg, store = _engine_setup(seq=64)
+    model = cached_model(store)
+    assert isinstance(model, FusedCachedModel)
+    prefix = list(range(1, 40))
+    out = generate_ids(model, prefix, SampleOptions(max_tokens=40, temperature=0.0))
+    assert len(out) == 40  # slides past sequence_len (64) by re-prefilling the window
+    ref = ReferenceGpt(store, torch.float32)
+    first = int(ref.forward(torch.tensor([prefix]).cuda())[0, -1].argmax())
+    logits = ref.forward(torch.tensor([prefix]).cuda())[0, -1]
+    top2 = logits.topk(2).values
+    if float(top2[0] - top2[1]) > 0.05:  # a clear winner must agree
+        assert out[0] == first

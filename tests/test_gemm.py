@@ -64,3 +64,16 @@ def test_residual_in_place():
     ref = r.float() + x.float() @ w.float().t()
     gemm.linear_residual(x, w, r, out=r)
     _close(r, ref)
+
+
+@pytest.mark.parametrize("m", [1, 3, 64])
+def test_skinny_m_all_forward_epilogues(m):
+    """Decode-sized GEMMs: fewer token rows than one 128-row tile."""
+    from rs_nanogpt_b200.ops import gemm
+    torch.manual_seed(5)
+    x, w, r = _rand(m, 256), _rand(512, 256), _rand(m, 512)
+    _close(gemm.linear(x, w), x.float() @ w.float().t())
+    ref = r.float() + x.float() @ w.float().t()
+    _close(gemm.linear_residual(x, w, r), ref)
+    act, h = gemm.linear_relu2(x, w)
+    _close(h, x.float() @ w.float().t())
