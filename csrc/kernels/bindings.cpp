@@ -44,6 +44,10 @@ void decode_attention(torch::Tensor qkv, torch::Tensor k_cache, torch::Tensor v_
 void sample_tokens(torch::Tensor logits, double temperature, int64_t top_k, torch::Tensor uniforms,
                    torch::Tensor gen_count, torch::Tensor out_tokens, torch::Tensor next_in, torch::Tensor pos,
                    bool advance_pos);
+void skinny_finish(torch::Tensor acc, torch::Tensor out, int64_t mode, c10::optional<torch::Tensor> aux,
+                   c10::optional<torch::Tensor> aux_out, c10::optional<torch::Tensor> norm_out, double eps);
+void qkv_decode_finish(torch::Tensor acc, torch::Tensor qkv, torch::Tensor k_cache, torch::Tensor v_cache,
+                       torch::Tensor pos, torch::Tensor cos_t, torch::Tensor sin_t, int64_t H, double eps);
 }  // namespace nk
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -73,4 +77,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kv_rope_append", &nk::kv_rope_append);
   m.def("decode_attention", &nk::decode_attention);
   m.def("sample_tokens", &nk::sample_tokens);
+  m.def("skinny_finish", &nk::skinny_finish);
+  m.def("qkv_decode_finish", &nk::qkv_decode_finish);
 }

@@ -222,15 +222,16 @@ __global__ void decode_combine_kernel(const float* __restrict__ part_o, const fl
 
 // ---- sampling ------------------------------------------------------------------
 
-constexpr int kSampThreads = 1024;
+constexpr int kSampThreads = 512;
 
 __device__ __forceinline__ uint32_t bf16_order_key(uint16_t u) {
   return (u & 0x8000u) ? (~uint32_t(u) & 0xFFFFu) : (uint32_t(u) | 0x8000u);
 }
 
 // Exclusive block scan (double) over kSampThreads threads; returns the prefix
-// and writes the block total to *total (visible to all threads on return).
+// and writes the block total to *total.
 __device__ double block_excl_scan(double v, double* sm_warp, double* total) {
+  constexpr int kWarps = kSampThreads / 32;
   const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
   double x = v;
 #pragma unroll
@@ -241,45 +242,81 @@ __device__ double block_excl_scan(double v, double* sm_warp, double* total) {
   if (lane == 31) sm_warp[warp] = x;
   __syncthreads();
   if (warp == 0) {
-    double w = sm_warp[lane];
+    double w = lane < kWarps ? sm_warp[lane] : 0.0;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const double y = __shfl_up_sync(0xffffffffu, w, o);
       if (lane >= o) w += y;
     }
-    sm_warp[lane] = w;  // inclusive warp totals
+    if (lane < kWarps) sm_warp[lane] = w;  // inclusive warp totals
   }
   __syncthreads();
   const double before = (warp ? sm_warp[warp - 1] : 0.0) + x - v;
-  *total = sm_warp[31];
+  *total = sm_warp[kWarps - 1];
   __syncthreads();
   return before;
 }
 
-// One CTA per row. Step index of row b is gen_count[b]; its uniform is
-// uniforms[step * B + b]; the token goes to out_tokens[b * max_steps + step]
-// and next_in[b]; gen_count[b] advances, and pos[b] too when advance_pos.
+// Block-wide sum of an int (every thread gets the total).
+__device__ __forceinline__ int block_sum_int(int v, int* sm) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if (threadIdx.x % 32 == 0) sm[threadIdx.x / 32] = v;
+  __syncthreads();
+  int t = 0;
+#pragma unroll
+  for (int w = 0; w < kSampThreads / 32; ++w) t += sm[w];
+  __syncthreads();
+  return t;
+}
+
+// One CTA per row. Thread t owns the contiguous logits [t*VPT, t*VPT + VPT)
+// (so per-thread sums in index order can be block-scanned); their 16-bit
+// order keys live in shared memory, two per word, with thread t's word j at
+// t*W + (j ^ (t % 32)) (W = VPT/2, a multiple of 32) so that the 32 lanes of
+// a warp reading their j-th words hit 32 different banks.
+// Step index of row b is gen_count[b]; its uniform is uniforms[step * B + b];
+// the token goes to out_tokens[b * max_steps + step] and next_in[b];
+// gen_count[b] advances, and pos[b] too when advance_pos.
+// The k-th largest key (tau) is found by a 16-step binary search over the key
+// space, each step counting keys >= mid.
 __global__ void __launch_bounds__(kSampThreads) sample_tokens_kernel(
-    const __nv_bfloat16* __restrict__ logits, int ld, int V, float temperature, int top_k,
+    const __nv_bfloat16* __restrict__ logits, int ld, int V, int VPT, float temperature, int top_k,
     const double* __restrict__ uniforms, int B, int max_steps, int* __restrict__ gen_count,
     int* __restrict__ out_tokens, int64_t* __restrict__ next_in, int* __restrict__ pos, int advance_pos) {
+  extern __shared__ uint32_t keys[];
   const int b = blockIdx.x, tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
-  const uint16_t* row = reinterpret_cast<const uint16_t*>(logits + long(b) * ld);
-  const int seg = (V + kSampThreads - 1) / kSampThreads;
-  const int i0 = min(V, tid * seg), i1 = min(V, i0 + seg);
-  __shared__ uint32_t hist[256];
+  const int W = VPT / 2, i0 = tid * VPT, sw = tid & 31;
+  const uint32_t* mine = keys + tid * W;
   __shared__ double sm_scan[32];
-  __shared__ float sm_f[32];
-  __shared__ int sm_i[32];
-  __shared__ uint32_t sm_sel[4];  // threshold key, quota, token
+  __shared__ int sm_int[32];
+  __shared__ uint32_t sm_key[32];
+  __shared__ int sm_idx[32];
   __shared__ int sm_token;
 
-  // Largest value (order key) and the last index holding it.
+  {
+    const uint16_t* row = reinterpret_cast<const uint16_t*>(logits + long(b) * ld);
+    const int words = kSampThreads * W;
+    for (int g = tid; g < words; g += kSampThreads) {
+      const int i = 2 * g;
+      const uint32_t lo = i < V ? bf16_order_key(row[i]) : 0u;
+      const uint32_t hi = i + 1 < V ? bf16_order_key(row[i + 1]) : 0u;
+      const int t = g / W, j = g % W;
+      keys[t * W + (j ^ (t & 31))] = lo | (hi << 16);
+    }
+  }
+  __syncthreads();
+#define KEYW(j) mine[(j) ^ sw]
+
+  // Largest key, last index on ties.
   uint32_t best = 0;
   int best_i = -1;
-  for (int i = i0; i < i1; ++i) {
-    const uint32_t k = bf16_order_key(row[i]);
-    if (k >= best) { best = k; best_i = i; }
+  for (int j = 0; j < W; ++j) {
+    const uint32_t w = KEYW(j);
+    const uint32_t lo = w & 0xFFFFu, hi = w >> 16;
+    const int i = i0 + 2 * j;
+    if (i < V && lo >= best) { best = lo; best_i = i; }
+    if (i + 1 < V && hi >= best) { best = hi; best_i = i + 1; }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -287,112 +324,222 @@ __global__ void __launch_bounds__(kSampThreads) sample_tokens_kernel(
     const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
     if (ok > best || (ok == best && oi > best_i)) { best = ok; best_i = oi; }
   }
-  if (lane == 0) { sm_i[warp] = best_i; sm_f[warp] = __uint_as_float(best); }
+  if (lane == 0) { sm_key[warp] = best; sm_idx[warp] = best_i; }
   __syncthreads();
   if (warp == 0) {
-    best = __float_as_uint(sm_f[lane]);
-    best_i = sm_i[lane];
+    best = lane < kSampThreads / 32 ? sm_key[lane] : 0u;
+    best_i = lane < kSampThreads / 32 ? sm_idx[lane] : -1;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const uint32_t ok = __shfl_xor_sync(0xffffffffu, best, o);
       const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
       if (ok > best || (ok == best && oi > best_i)) { best = ok; best_i = oi; }
     }
-    if (lane == 0) { sm_sel[3] = best; sm_token = best_i; }
+    if (lane == 0) { sm_key[0] = best; sm_token = best_i; }
   }
   __syncthreads();
-  const uint32_t max_key = sm_sel[3];
+  const uint32_t max_key = sm_key[0];
   const int step = gen_count[b];
 
   if (temperature > 0.f) {
-    // Threshold key tau and how many logits equal to tau are kept.
     const bool all = top_k <= 0 || top_k >= V;
-    uint32_t tau = 0, quota = 0xFFFFFFFFu;
+    uint32_t tau = 0;
+    int quota = 0x7FFFFFFF;
     if (!all) {
-      for (int i = tid; i < 256; i += kSampThreads) hist[i] = 0;
-      __syncthreads();
-      for (int i = i0; i < i1; ++i) atomicAdd(&hist[bf16_order_key(row[i]) >> 8], 1u);
-      __syncthreads();
-      if (tid == 0) {
-        uint32_t cum = 0;
-        int hb = 255;
-        for (; hb > 0; --hb) {
-          if (cum + hist[hb] >= uint32_t(top_k)) break;
-          cum += hist[hb];
+      // Largest tau with count(key >= tau) >= k (padding keys are 0 and
+      // real keys are >= 1, so padding never reaches the count at tau >= 1).
+      uint32_t lo = 1, hi = 0xFFFFu;
+      while (lo < hi) {
+        const uint32_t mid = (lo + hi + 1) >> 1;
+        int cnt = 0;
+        for (int j = 0; j < W; ++j) {
+          const uint32_t w = KEYW(j);
+          cnt += ((w & 0xFFFFu) >= mid) + ((w >> 16) >= mid);
         }
-        sm_sel[0] = uint32_t(hb);
-        sm_sel[1] = cum;
+        if (block_sum_int(cnt, sm_int) >= top_k) lo = mid;
+        else hi = mid - 1;
       }
-      __syncthreads();
-      const uint32_t hb = sm_sel[0], above = sm_sel[1];
-      __syncthreads();
-      for (int i = tid; i < 256; i += kSampThreads) hist[i] = 0;
-      __syncthreads();
-      for (int i = i0; i < i1; ++i) {
-        const uint32_t k = bf16_order_key(row[i]);
-        if ((k >> 8) == hb) atomicAdd(&hist[k & 255u], 1u);
+      tau = lo;
+      int gt = 0;
+      for (int j = 0; j < W; ++j) {
+        const uint32_t w = KEYW(j);
+        gt += ((w & 0xFFFFu) > tau) + ((w >> 16) > tau);
       }
-      __syncthreads();
-      if (tid == 0) {
-        uint32_t cum = above;
-        int lb = 255;
-        for (; lb > 0; --lb) {
-          if (cum + hist[lb] >= uint32_t(top_k)) break;
-          cum += hist[lb];
-        }
-        sm_sel[0] = (hb << 8) | uint32_t(lb);
-        sm_sel[1] = uint32_t(top_k) - cum;  // ties at tau that are kept
-      }
-      __syncthreads();
-      tau = sm_sel[0];
-      quota = sm_sel[1];
+      quota = top_k - block_sum_int(gt, sm_int);  // ties at tau that are kept, lowest index first
     }
-    // Rank of this thread's first tie among all ties (index order).
     int ties = 0;
     if (!all)
-      for (int i = i0; i < i1; ++i) ties += bf16_order_key(row[i]) == tau;
+      for (int j = 0; j < W; ++j) {
+        const uint32_t w = KEYW(j);
+        ties += ((w & 0xFFFFu) == tau) + ((w >> 16) == tau);
+      }
     double tie_total;
-    const double tie_before = block_excl_scan(double(ties), sm_scan, &tie_total);
-    const float mx = __bfloat162float(__ushort_as_bfloat16(uint16_t((max_key & 0x8000u) ? (max_key & 0x7FFFu)
-                                                                                          : (~max_key & 0xFFFFu))));
+    const int tie_before = int(block_excl_scan(double(ties), sm_scan, &tie_total));
+    const float mx = __bfloat162float(__ushort_as_bfloat16(
+        uint16_t((max_key & 0x8000u) ? (max_key & 0x7FFFu) : (~max_key & 0xFFFFu))));
     const float sc = kLog2e / temperature;
-    float wsum = 0.f;
-    int rank = int(tie_before);
-    for (int i = i0; i < i1; ++i) {
-      const uint32_t k = bf16_order_key(row[i]);
+    // Kept-logit weight exp((x - max) / T), in base 2.
+    auto weight = [&](uint32_t k, int i, int& rank_io) -> float {
+      if (i >= V) return 0.f;
       bool keep = all || k > tau;
-      if (!all && k == tau) keep = uint32_t(rank++) < quota;
-      if (keep) wsum += exp2f((__bfloat162float(__ushort_as_bfloat16(row[i])) - mx) * sc);
+      if (!all && k == tau) keep = rank_io++ < quota;
+      if (!keep) return 0.f;
+      const uint16_t u = uint16_t((k & 0x8000u) ? (k & 0x7FFFu) : (~k & 0xFFFFu));
+      return exp2f((__bfloat162float(__ushort_as_bfloat16(u)) - mx) * sc);
+    };
+    float wsum = 0.f;
+    int rank = tie_before;
+    for (int j = 0; j < W; ++j) {
+      const uint32_t w = KEYW(j);
+      wsum += weight(w & 0xFFFFu, i0 + 2 * j, rank);
+      wsum += weight(w >> 16, i0 + 2 * j + 1, rank);
     }
     double total;
     const double before = block_excl_scan(double(wsum), sm_scan, &total);
     const double u = uniforms[long(step < max_steps ? step : max_steps - 1) * B + b];
     const double thr = u * total;
-    if (wsum > 0.f && thr >= before && (thr < before + double(wsum) || tid == kSampThreads - 1 ||
-                                        before + double(wsum) >= total)) {
+    // The thread whose interval [before, before + wsum) holds thr picks; the
+    // last thread with weight also takes thr values lost to rounding.
+    if (wsum > 0.f && thr >= before && (thr < before + double(wsum) || before + double(wsum) >= total)) {
       double acc = before;
       int pick = -1, last = -1;
-      rank = int(tie_before);
-      for (int i = i0; i < i1; ++i) {
-        const uint32_t k = bf16_order_key(row[i]);
-        bool keep = all || k > tau;
-        if (!all && k == tau) keep = uint32_t(rank++) < quota;
-        if (!keep) continue;
-        last = i;
-        acc += double(exp2f((__bfloat162float(__ushort_as_bfloat16(row[i])) - mx) * sc));
-        if (acc > thr) { pick = i; break; }
+      rank = tie_before;
+      for (int e = 0; e < VPT && pick < 0; ++e) {
+        const uint32_t w = KEYW(e >> 1);
+        const float x = weight((e & 1) ? (w >> 16) : (w & 0xFFFFu), i0 + e, rank);
+        if (x > 0.f) {
+          last = i0 + e;
+          acc += double(x);
+          if (acc > thr) pick = i0 + e;
+        }
       }
-      if (pick < 0) pick = last;
-      sm_token = pick;  // at most one thread's interval holds thr
+      sm_token = pick >= 0 ? pick : last;
     }
     __syncthreads();
   }
+#undef KEYW
   if (tid == 0) {
     const int tok = sm_token;
     if (step < max_steps) out_tokens[long(b) * max_steps + step] = tok;
     next_in[b] = tok;
     gen_count[b] = step + 1;
     if (advance_pos) pos[b] += 1;
+  }
+}
+
+// ---- skinny GEMM epilogues -------------------------------------------------------
+
+// The decode-path GEMMs run with operands swapped (the weight rows fill the
+// 128-row tensor-core tile and the grid; the few token rows are the narrow N
+// side), split over K with fp32 atomics straight into acc[M, N] (token-major).
+// These kernels read one token row of the accumulator per CTA, zero it for the
+// next product and apply the epilogue.
+
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16(x)); }
+
+// mode 0: out = acc; 1: out = relu(acc)^2 (aux_out = acc when given);
+// 3: out = acc + aux. With norm_out, also norm_out = RMSNorm(out) (N <= 2048).
+constexpr int kFinThreads = 128;
+constexpr int kFinKeep = 4;  // float4 chunks per thread kept for the norm
+
+__global__ void __launch_bounds__(kFinThreads) skinny_finish_kernel(
+    float* __restrict__ acc, int N, int mode, __nv_bfloat16* __restrict__ out, int ld_out,
+    const __nv_bfloat16* __restrict__ aux, int ld_aux, __nv_bfloat16* __restrict__ aux_out, int ld_aux_out,
+    __nv_bfloat16* __restrict__ norm_out, int ld_norm, float eps) {
+  const int m = blockIdx.x, tid = threadIdx.x;
+  float4* a = reinterpret_cast<float4*>(acc + long(m) * N);
+  auto process = [&](int c4) -> float4 {
+    const float4 v = a[c4];
+    a[c4] = make_float4(0.f, 0.f, 0.f, 0.f);
+    float x[4] = {bf16r(v.x), bf16r(v.y), bf16r(v.z), bf16r(v.w)};
+    if (mode == 3) {
+      const uint2 r = *reinterpret_cast<const uint2*>(aux + long(m) * ld_aux + c4 * 4);
+      const float2 r0 = unpack_bf16x2(r.x), r1 = unpack_bf16x2(r.y);
+      x[0] = bf16r(x[0] + r0.x); x[1] = bf16r(x[1] + r0.y); x[2] = bf16r(x[2] + r1.x); x[3] = bf16r(x[3] + r1.y);
+    } else if (mode == 1) {
+      if (aux_out)
+        *reinterpret_cast<uint2*>(aux_out + long(m) * ld_aux_out + c4 * 4) =
+            make_uint2(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float h = fmaxf(x[i], 0.f);
+        x[i] = bf16r(h * h);
+      }
+    }
+    *reinterpret_cast<uint2*>(out + long(m) * ld_out + c4 * 4) =
+        make_uint2(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]));
+    return make_float4(x[0], x[1], x[2], x[3]);
+  };
+  float4 keep[kFinKeep];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kFinKeep; ++j) {
+    const int c4 = tid + j * kFinThreads;
+    keep[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c4 < N / 4) {
+      keep[j] = process(c4);
+      ss += keep[j].x * keep[j].x + keep[j].y * keep[j].y + keep[j].z * keep[j].z + keep[j].w * keep[j].w;
+    }
+  }
+  for (int c4 = tid + kFinKeep * kFinThreads; c4 < N / 4; c4 += kFinThreads) process(c4);  // no norm here
+  if (norm_out == nullptr) return;
+  __shared__ float red[kFinThreads / 32];
+  ss = dec_warp_sum(ss);
+  if (tid % 32 == 0) red[tid / 32] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < kFinThreads / 32; ++w) tot += red[w];
+  // The reference divides by the bf16-rounded denominator.
+  const float denom = bf16r(sqrtf(tot / N + eps));
+#pragma unroll
+  for (int j = 0; j < kFinKeep; ++j) {
+    const int c4 = tid + j * kFinThreads;
+    if (c4 >= N / 4) break;
+    const float4 x = keep[j];
+    *reinterpret_cast<uint2*>(norm_out + long(m) * ld_norm + c4 * 4) =
+        make_uint2(pack_bf16x2(x.x / denom, x.y / denom), pack_bf16x2(x.z / denom, x.w / denom));
+  }
+}
+
+// QKV epilogue of a decode step: acc[M, 3C] -> q (RoPE + QK-norm) into the
+// qkv buffer, k (RoPE + QK-norm) and v into the caches at position pos[m].
+// Warp per (part, head) item; 8 warps per token row.
+__global__ void __launch_bounds__(256) qkv_decode_finish_kernel(
+    float* __restrict__ acc, int H, int C, __nv_bfloat16* __restrict__ q_out, int ld_q,
+    __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc, const int* __restrict__ pos, int cap,
+    const float* __restrict__ cos_t, const float* __restrict__ sin_t, int max_pos, float eps) {
+  const int m = blockIdx.x, warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int p = pos[m];
+  const int pp = min(p, max_pos - 1);
+  for (int item = warp; item < 3 * H; item += 8) {
+    const int part = item / H, h = item % H;
+    float4* a = reinterpret_cast<float4*>(acc + long(m) * 3 * C + part * C + h * 128) + lane;
+    const float4 v = *a;
+    *a = make_float4(0.f, 0.f, 0.f, 0.f);
+    float x[4] = {bf16r(v.x), bf16r(v.y), bf16r(v.z), bf16r(v.w)};
+    if (part < 2) {
+      const bool first = lane < 16;
+      float o[4];
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const float partner = __shfl_xor_sync(0xffffffffu, x[jj], 16);
+        const int i = (lane & 15) * 4 + jj;
+        const float c = cos_t[pp * 64 + i], sn = sin_t[pp * 64 + i];
+        o[jj] = first ? x[jj] * c + partner * sn : x[jj] * c - partner * sn;
+      }
+      const float ss = dec_warp_sum(o[0] * o[0] + o[1] * o[1] + o[2] * o[2] + o[3] * o[3]);
+      const float denom = bf16r(sqrtf(ss / 128.f + eps));
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) x[jj] = o[jj] / denom;
+    }
+    const uint2 w = make_uint2(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]));
+    if (part == 0) {
+      *reinterpret_cast<uint2*>(q_out + long(m) * ld_q + h * 128 + lane * 4) = w;
+    } else if (p < cap) {
+      __nv_bfloat16* dst = (part == 1 ? kc : vc) + ((long(m) * H + h) * cap + p) * 128 + lane * 4;
+      *reinterpret_cast<uint2*>(dst) = w;
+    }
   }
 }
 
@@ -482,12 +629,81 @@ void sample_tokens(torch::Tensor logits, double temperature, int64_t top_k, torc
               "sample_tokens: out_tokens [B, max_steps] int32");
   TORCH_CHECK(next_in.scalar_type() == at::kLong && next_in.is_contiguous() && next_in.numel() >= B,
               "sample_tokens: next_in int64 [B]");
+  // Logits per thread: a multiple of 64 (32 key words, the swizzle period).
+  const int vpt = int(((V + kSampThreads - 1) / kSampThreads + 63) / 64 * 64);
+  const size_t smem = size_t(kSampThreads) * vpt * 2;
+  TORCH_CHECK(smem <= 200 * 1024, "sample_tokens: vocabulary too large for the shared-memory key table");
+  static size_t smem_set = 0;
+  if (smem > smem_set) {
+    TORCH_CHECK(cudaFuncSetAttribute(sample_tokens_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     int(smem)) == cudaSuccess,
+                "sample_tokens: shared-memory opt-in failed");
+    smem_set = smem;
+  }
   const at::cuda::CUDAGuard guard(logits.device());
-  sample_tokens_kernel<<<B, kSampThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), int(logits.stride(0)), int(V), float(temperature),
-      int(top_k), uniforms.data_ptr<double>(), int(B), int(max_steps), gen_count.data_ptr<int>(),
+  sample_tokens_kernel<<<B, kSampThreads, smem, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), int(logits.stride(0)), int(V), vpt,
+      float(temperature), int(top_k), uniforms.data_ptr<double>(), int(B), int(max_steps), gen_count.data_ptr<int>(),
       out_tokens.data_ptr<int>(), next_in.data_ptr<int64_t>(), pos.data_ptr<int>(), advance_pos ? 1 : 0);
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "sample_tokens launch failed");
+}
+
+void skinny_finish(torch::Tensor acc, torch::Tensor out, int64_t mode, c10::optional<torch::Tensor> aux,
+                   c10::optional<torch::Tensor> aux_out, c10::optional<torch::Tensor> norm_out, double eps) {
+  TORCH_CHECK(acc.is_cuda() && acc.scalar_type() == at::kFloat && acc.is_contiguous() && acc.dim() == 2,
+              "skinny_finish: acc is a contiguous fp32 [M, N] tensor");
+  const int64_t M = acc.size(0), N = acc.size(1);
+  TORCH_CHECK(N % 4 == 0, "skinny_finish: N must be a multiple of 4");
+  auto check_out = [&](const torch::Tensor& t, const char* what) {
+    TORCH_CHECK(t.scalar_type() == at::kBFloat16 && t.size(0) == M && t.size(1) == N && t.stride(1) == 1 &&
+                    t.stride(0) % 4 == 0,
+                "skinny_finish: ", what, " is bf16 [M, N] with 8-byte aligned rows");
+  };
+  check_out(out, "out");
+  TORCH_CHECK(mode == 0 || mode == 1 || mode == 3, "skinny_finish: mode 0, 1 or 3");
+  if (mode == 3) {
+    TORCH_CHECK(aux.has_value(), "skinny_finish: residual mode needs aux");
+    check_out(*aux, "aux");
+  }
+  if (aux_out) check_out(*aux_out, "aux_out");
+  if (norm_out) {
+    check_out(*norm_out, "norm_out");
+    TORCH_CHECK(N <= 4 * kFinThreads * kFinKeep, "skinny_finish: the fused norm takes N <= 2048");
+  }
+  const at::cuda::CUDAGuard guard(acc.device());
+  skinny_finish_kernel<<<M, kFinThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      acc.data_ptr<float>(), int(N), int(mode), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+      int(out.stride(0)), mode == 3 ? reinterpret_cast<const __nv_bfloat16*>(aux->data_ptr()) : nullptr,
+      mode == 3 ? int(aux->stride(0)) : 0,
+      (mode == 1 && aux_out) ? reinterpret_cast<__nv_bfloat16*>(aux_out->data_ptr()) : nullptr,
+      aux_out ? int(aux_out->stride(0)) : 0,
+      norm_out ? reinterpret_cast<__nv_bfloat16*>(norm_out->data_ptr()) : nullptr,
+      norm_out ? int(norm_out->stride(0)) : 0, float(eps));
+  TORCH_CHECK(cudaGetLastError() == cudaSuccess, "skinny_finish launch failed");
+}
+
+void qkv_decode_finish(torch::Tensor acc, torch::Tensor qkv, torch::Tensor k_cache, torch::Tensor v_cache,
+                       torch::Tensor pos, torch::Tensor cos_t, torch::Tensor sin_t, int64_t H, double eps) {
+  TORCH_CHECK(acc.is_cuda() && acc.scalar_type() == at::kFloat && acc.is_contiguous() && acc.dim() == 2,
+              "qkv_decode_finish: acc is a contiguous fp32 [M, 3C] tensor");
+  const int64_t M = acc.size(0), C = acc.size(1) / 3;
+  TORCH_CHECK(C == H * 128, "qkv_decode_finish: head_dim must be 128");
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.size(0) == M && qkv.size(1) >= C && qkv.stride(1) == 1 &&
+                  qkv.stride(0) % 4 == 0,
+              "qkv_decode_finish: q output rows");
+  TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous() && k_cache.sizes() == v_cache.sizes() &&
+                  k_cache.size(0) >= M && k_cache.size(1) == H && k_cache.size(3) == 128 &&
+                  k_cache.scalar_type() == at::kBFloat16 && v_cache.scalar_type() == at::kBFloat16,
+              "qkv_decode_finish: caches are bf16 [B, H, capacity, 128]");
+  check_i32(pos, M, "qkv_decode_finish pos");
+  TORCH_CHECK(cos_t.is_contiguous() && sin_t.is_contiguous() && cos_t.size(1) == 64, "qkv_decode_finish: tables");
+  const at::cuda::CUDAGuard guard(acc.device());
+  qkv_decode_finish_kernel<<<M, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      acc.data_ptr<float>(), int(H), int(C), reinterpret_cast<__nv_bfloat16*>(qkv.data_ptr()), int(qkv.stride(0)),
+      reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()), reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()),
+      pos.data_ptr<int>(), int(k_cache.size(2)), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),
+      int(cos_t.size(0)), float(eps));
+  TORCH_CHECK(cudaGetLastError() == cudaSuccess, "qkv_decode_finish launch failed");
 }
 
 }  // namespace nk

@@ -34,6 +34,7 @@ enum GemmMode : int {
   kResidual = 3,    // C = alpha*acc + AUX (AUX may alias C)
   kAtomicF32 = 4,   // C(fp32) += alpha*acc   (split-K capable)
   kRopeNorm = 5,    // QKV projection: q and k heads get RoPE + RMSNorm over head_dim, v stored plain
+  kAtomicF32T = 6,  // C^T(fp32) += alpha*acc: C is [N, M]; a warp's 32 rows hit 32 adjacent floats
 };
 
 struct GemmArgs {
@@ -130,6 +131,17 @@ __device__ __forceinline__ void atomic_chunk(const GemmArgs& a, int row, int col
   } else {
     for (int i = 0; i < 32 && col0 + i < a.N; ++i) atomicAdd(c + i, a.alpha * v[i]);
   }
+}
+
+// Transposed accumulation: element (row, col) goes to C[col * ldc + row]. The
+// 32 lanes of a warp hold 32 consecutive rows, so each red.add covers one
+// contiguous 128-byte line.
+__device__ __forceinline__ void atomic_chunk_t(const GemmArgs& a, int row, int col0, const float (&v)[32]) {
+  if (row >= a.M) return;
+  float* c = reinterpret_cast<float*>(a.C) + row;
+#pragma unroll
+  for (int i = 0; i < 32; ++i)
+    if (col0 + i < a.N) atomicAdd(c + long(col0 + i) * a.ldc, a.alpha * v[i]);
 }
 
 template <int BN>
@@ -235,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = ew / 4;                // which half of the tile's columns
     uint8_t* buf_o = staging + ew * 2 * kStageBufBytes;
     uint8_t* buf_x = buf_o + kStageBufBytes;
-    const bool atomic = args.mode == kAtomicF32;
+    const bool atomic = args.mode == kAtomicF32 || args.mode == kAtomicF32T;
     const bool need_aux = args.mode == kResidual || args.mode == kDRelu2;
     uint32_t aux_phase = 0;
     bool ok = true;
@@ -308,7 +320,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         float v[32];
         tmem_ld_32x32(tmem_base + (uint32_t(q * 32) << 16) + b * BN + c * 32, v);
         if (atomic) {
-          atomic_chunk(args, row0 + lane, col0, v);
+          if (args.mode == kAtomicF32T) atomic_chunk_t(args, row0 + lane, col0, v);
+          else atomic_chunk(args, row0 + lane, col0, v);
           continue;
         }
         float x[32];
@@ -408,9 +421,11 @@ void gemm_impl(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_majo
   const int K = int(a_mn_major ? A.size(0) : A.size(1));
   const int N = int(b_mn_major ? B.size(1) : B.size(0));
   TORCH_CHECK((b_mn_major ? B.size(0) : B.size(1)) == K, "gemm: K mismatch");
-  TORCH_CHECK(C.size(0) == M && C.size(1) == N, "gemm: C shape mismatch");
+  const bool c_transposed = mode == kAtomicF32T;
+  TORCH_CHECK(c_transposed ? (C.size(0) == N && C.size(1) == M) : (C.size(0) == M && C.size(1) == N),
+              "gemm: C shape mismatch");
   TORCH_CHECK(M > 0 && N > 0 && K > 0, "gemm: empty problem");
-  const bool f32out = mode == kAtomicF32;
+  const bool f32out = mode == kAtomicF32 || mode == kAtomicF32T;
   TORCH_CHECK(C.scalar_type() == (f32out ? at::kFloat : at::kBFloat16), "gemm: C dtype does not fit the mode");
   TORCH_CHECK(splits == 1 || f32out, "gemm: split-K needs the atomic fp32 mode");
   const int elt = f32out ? 4 : 2;

@@ -67,6 +67,9 @@ class DecodeEngine:
         splits = (capacity + chunk - 1) // chunk
         self.part_o = torch.empty(batch * h * splits * 128, **f32)
         self.part_ml = torch.empty(batch * h * splits * 2, **f32)
+        # Swapped-operand split-K GEMMs for the block weights (see gemm.linear_skinny).
+        self.skinny = gemm.skinny_ok(batch)
+        self.acc = torch.zeros(4 * c * batch, **f32) if self.skinny else None  # zero between products
         self.out_tokens = None
         self.uniforms = None
         self._graph = None
@@ -105,20 +108,34 @@ class DecodeEngine:
         cfg, st, m = self.cfg, self.store, self.model
         eps = cfg.norm_eps
         x = L.embedding(self.next_in, st.work_of("wte.weight"), out=self.x)
+        L.rmsnorm(x, eps, out=self.h)
         for i in range(cfg.n_layer):
             p = f"blocks.{i}."
-            L.rmsnorm(x, eps, out=self.h)
-            gemm.linear(self.h, st.qkv_work(i), out=self.qkv)
-            L.kv_rope_append(self.qkv, self.k_cache[i], self.v_cache[i], self.pos, None, 1, cfg.n_head, m.cos,
-                             m.sin, True, eps)
+            if self.skinny:
+                # Each GEMM's epilogue also does the following elementwise op:
+                # RoPE/QK-norm + cache append, residual + the next RMSNorm.
+                gemm.linear_qkv_decode(self.h, st.qkv_work(i), self.acc, self.qkv, self.k_cache[i], self.v_cache[i],
+                                       self.pos, m.cos, m.sin, cfg.n_head, eps)
+            else:
+                gemm.linear(self.h, st.qkv_work(i), out=self.qkv)
+                L.kv_rope_append(self.qkv, self.k_cache[i], self.v_cache[i], self.pos, None, 1, cfg.n_head, m.cos,
+                                 m.sin, True, eps)
             L.decode_attention(self.qkv, self.k_cache[i], self.v_cache[i], self.pos, self.y, self.part_o,
                                self.part_ml, self.chunk)
-            gemm.linear_residual(self.y, st.work_of(p + "attn.c_proj.weight"), x, out=self.xmid)
-            L.rmsnorm(self.xmid, eps, out=self.h)
-            gemm.linear_relu2(self.h, st.work_of(p + "mlp.c_fc.weight"), act=self.act, h=self.hpre)
-            gemm.linear_residual(self.act, st.work_of(p + "mlp.c_proj.weight"), self.xmid, out=x)
-        L.rmsnorm(x, eps, out=self.h)
-        gemm.linear(self.h, st.work_of("lm_head.weight"), out=self.logits)
+            w_proj, w_fc, w_mlp = (st.work_of(p + n) for n in
+                                   ("attn.c_proj.weight", "mlp.c_fc.weight", "mlp.c_proj.weight"))
+            if self.skinny:
+                gemm.linear_skinny(self.y, w_proj, self.acc, self.xmid, gemm.RESIDUAL, aux=x, norm_out=self.h, eps=eps)
+                gemm.linear_skinny(self.h, w_fc, self.acc, self.act, gemm.RELU2)
+                gemm.linear_skinny(self.act, w_mlp, self.acc, x, gemm.RESIDUAL, aux=self.xmid, norm_out=self.h,
+                                   eps=eps)
+            else:
+                gemm.linear_residual(self.y, w_proj, x, out=self.xmid)
+                L.rmsnorm(self.xmid, eps, out=self.h)
+                gemm.linear_relu2(self.h, w_fc, act=self.act, h=self.hpre)
+                gemm.linear_residual(self.act, w_mlp, self.xmid, out=x)
+                L.rmsnorm(x, eps, out=self.h)
+        gemm.linear(self.h, st.work_of("lm_head.weight"), out=self.logits)  # h = final norm of x
         return self.logits
 
     # ---- on-device sampling ----------------------------------------------------------

@@ -82,6 +82,51 @@ def linear_dgrad_drelu2(dy, w, h, out=None):
     return out
 
 
+ATOMIC_F32_T = 6
+
+
+def skinny_ok(m: int) -> bool:
+    """Whether ``linear_skinny`` is meant for ``m`` token rows (decode sizes)."""
+    return 0 < m <= 256
+
+
+def _skinny_acc(x, w, acc, splits: int):
+    """acc[M,N] (fp32, zero on entry) += x w^T with swapped operands: the
+    weight rows fill the 128-row tensor-core tile and the grid, the few token
+    rows are the narrow side, and K is split across the SMs (fp32 atomics,
+    each warp's adds covering contiguous 128-byte lines)."""
+    m, k = x.shape
+    n = w.shape[0]
+    c = acc[: m * n].view(m, n)
+    if splits <= 0:
+        tiles = (n + 127) // 128
+        splits = max(1, min((k + 63) // 64, _sms() // tiles))
+    ext().gemm(w, False, x, False, c, ATOMIC_F32_T, 1.0, None, None, splits, 128)
+    return c
+
+
+def linear_skinny(x, w, acc, out, mode: int = STORE, aux=None, aux_out=None, norm_out=None, eps: float = 0.0,
+                  splits: int = 0):
+    """Decode-sized product out[M,N] (op)= x[M,K] w[N,K]^T.
+
+    The epilogue kernel reads the fp32 accumulator row by row, zeroes it and
+    applies STORE, RELU2 (``aux_out`` = pre-activation, optional) or RESIDUAL
+    (``aux`` added); with ``norm_out`` it also writes RMSNorm(out) (the next
+    layer's input) in the same pass."""
+    c = _skinny_acc(x, w, acc, splits)
+    ext().skinny_finish(c, out, mode, aux, aux_out, norm_out, eps)
+    return out
+
+
+def linear_qkv_decode(x, w_qkv, acc, qkv, k_cache, v_cache, pos, cos, sin, n_head: int, eps: float,
+                      splits: int = 0):
+    """Decode-step QKV projection: q gets RoPE + QK-norm into ``qkv[:, :C]``;
+    k (RoPE + QK-norm) and v go straight into the layer's caches at ``pos``."""
+    c = _skinny_acc(x, w_qkv, acc, splits)
+    ext().qkv_decode_finish(c, qkv, k_cache, v_cache, pos, cos, sin, n_head, eps)
+    return qkv
+
+
 def linear_wgrad(dy, x, grad, alpha: float = 1.0, splits: int = 0):
     """grad[N,K] (fp32) += alpha * dy[M,N]^T @ x[M,K].
 

@@ -194,3 +194,28 @@ def test_fused_cached_model_greedy_generation():
     top2 = logits.topk(2).values
     if float(top2[0] - top2[1]) > 0.05:  # a clear winner must agree
         assert out[0] == first
+
+
+def test_qkv_decode_gemm_matches_separate_kernels():
+    """Decode QKV GEMM with the RoPE/QK-norm + cache-append epilogue vs the
+    plain GEMM followed by kv_rope_append."""
+    from rs_nanogpt_b200.ops import gemm
+    from rs_nanogpt_b200.ops import layers as L
+    torch.manual_seed(7)
+    b, h, cap = 6, 2, 40
+    c = h * 128
+    cos, sin = _tables(h)
+    x = torch.randn(b, c, device="cuda").bfloat16()
+    w = (torch.randn(3 * c, c, device="cuda") * 0.05).bfloat16()
+    pos = torch.tensor([0, 3, 39, 17, 8, 1], device="cuda", dtype=torch.int32)
+    k1, v1 = (torch.zeros(b, h, cap, 128, device="cuda", dtype=torch.bfloat16) for _ in range(2))
+    k2, v2 = torch.zeros_like(k1), torch.zeros_like(v1)
+    q1 = gemm.linear(x, w)
+    L.kv_rope_append(q1, k1, v1, pos, None, 1, h, cos, sin, True, 1e-6)
+    acc = torch.zeros(b * 3 * c, device="cuda")
+    q2 = torch.zeros(b, 3 * c, device="cuda", dtype=torch.bfloat16)
+    gemm.linear_qkv_decode(x, w, acc, q2, k2, v2, pos, cos, sin, h, 1e-6)
+    _close(q2[:, :c], q1[:, :c], 2e-2)
+    _close(k2, k1, 2e-2)
+    _close(v2, v1, 2e-2)
+    assert acc.abs().sum().item() == 0

@@ -77,3 +77,26 @@ def test_skinny_m_all_forward_epilogues(m):
     _close(gemm.linear_residual(x, w, r), ref)
     act, h = gemm.linear_relu2(x, w)
     _close(h, x.float() @ w.float().t())
+
+
+@pytest.mark.parametrize("m", [1, 4, 64, 200])
+def test_linear_skinny_swapped_split_k(m):
+    """Decode GEMMs: swapped operands, split-K fp32 accumulation, row epilogues."""
+    from rs_nanogpt_b200.models.reference import rms_norm
+    from rs_nanogpt_b200.ops import gemm
+    torch.manual_seed(6)
+    k, n = 1280, 640
+    x, w, r = _rand(m, k), _rand(n, k, scale=0.05), _rand(m, n)
+    acc = torch.zeros(n * m, device="cuda")
+    ref = x.float() @ w.float().t()
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    _close(gemm.linear_skinny(x, w, acc, out), ref)
+    assert acc.abs().sum().item() == 0  # left zeroed for the next product
+    h = torch.empty_like(out)
+    gemm.linear_skinny(x, w, acc, out, gemm.RESIDUAL, aux=r, norm_out=h, eps=1e-6)
+    _close(out, r.float() + ref)
+    _close(h, rms_norm(out.float(), 1e-6))
+    pre = torch.empty_like(out)
+    gemm.linear_skinny(x, w, acc, out, gemm.RELU2, aux_out=pre)
+    _close(pre, ref)
+    _close(out, torch.relu(pre.float()) ** 2)
