@@ -43,7 +43,8 @@ def parse():
     p.add_argument("--device-batch", type=int, default=32)
     p.add_argument("--seq", type=int, default=2048)
     p.add_argument("--total-batch", type=int, default=TOTAL_BATCH)
-    p.add_argument("--backend", choices=["nccl", "fused"], default="nccl")
+    p.add_argument("--backend", choices=["nccl", "fused"], default="fused",
+                   help="fused: the P2P reduce-scatter + AdamW + all-gather kernel; nccl: the NCCL all-reduce baseline")
     p.add_argument("--no-e2e", action="store_true")
     return p.parse_args()
 

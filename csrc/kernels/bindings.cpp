@@ -48,6 +48,8 @@ void skinny_finish(torch::Tensor acc, torch::Tensor out, int64_t mode, c10::opti
                    c10::optional<torch::Tensor> aux_out, c10::optional<torch::Tensor> norm_out, double eps);
 void qkv_decode_finish(torch::Tensor acc, torch::Tensor qkv, torch::Tensor k_cache, torch::Tensor v_cache,
                        torch::Tensor pos, torch::Tensor cos_t, torch::Tensor sin_t, int64_t H, double eps);
+void gemm_skinny_acc(torch::Tensor w, torch::Tensor x, torch::Tensor acc, int64_t splits);
+void set_pdl(bool on);
 }  // namespace nk
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -79,4 +81,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample_tokens", &nk::sample_tokens);
   m.def("skinny_finish", &nk::skinny_finish);
   m.def("qkv_decode_finish", &nk::qkv_decode_finish);
+  m.def("gemm_skinny_acc", &nk::gemm_skinny_acc);
+  m.def("set_pdl", &nk::set_pdl, "programmatic dependent launch for the decode-chain kernels");
 }

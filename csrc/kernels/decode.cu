@@ -25,6 +25,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "launch.h"
 
 namespace nk {
 namespace {
@@ -107,6 +108,9 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
     const __nv_bfloat16* __restrict__ qkv, int ld_qkv, const __nv_bfloat16* __restrict__ kc,
     const __nv_bfloat16* __restrict__ vc, const int* __restrict__ pos, int H, int cap, int chunk, float scale_log2,
     float* __restrict__ part_o, float* __restrict__ part_ml, __nv_bfloat16* __restrict__ out, int ld_out) {
+  // No early trigger: this grid spans many waves, and a dependent GEMM's
+  // CTAs (a whole SM's shared memory each) would take SMs from it.
+  pdl_wait();
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z, S = gridDim.x;
   const int len = min(pos[b] + 1, cap);
   const int k0 = split * chunk, k1 = min(len, k0 + chunk);
@@ -205,6 +209,8 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
 __global__ void decode_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
                                       const int* __restrict__ pos, int H, int S, int chunk, int cap,
                                       __nv_bfloat16* __restrict__ out, int ld_out) {
+  pdl_trigger();
+  pdl_wait();
   const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
   const int len = min(pos[b] + 1, cap);
   const int used = min(S, (len + chunk - 1) / chunk);
@@ -284,6 +290,8 @@ __global__ void __launch_bounds__(kSampThreads) sample_tokens_kernel(
     const __nv_bfloat16* __restrict__ logits, int ld, int V, int VPT, float temperature, int top_k,
     const double* __restrict__ uniforms, int B, int max_steps, int* __restrict__ gen_count,
     int* __restrict__ out_tokens, int64_t* __restrict__ next_in, int* __restrict__ pos, int advance_pos) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ uint32_t keys[];
   const int b = blockIdx.x, tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
   const int W = VPT / 2, i0 = tid * VPT, sw = tid & 31;
@@ -446,6 +454,8 @@ __global__ void __launch_bounds__(kFinThreads) skinny_finish_kernel(
     float* __restrict__ acc, int N, int mode, __nv_bfloat16* __restrict__ out, int ld_out,
     const __nv_bfloat16* __restrict__ aux, int ld_aux, __nv_bfloat16* __restrict__ aux_out, int ld_aux_out,
     __nv_bfloat16* __restrict__ norm_out, int ld_norm, float eps) {
+  pdl_trigger();
+  pdl_wait();
   const int m = blockIdx.x, tid = threadIdx.x;
   float4* a = reinterpret_cast<float4*>(acc + long(m) * N);
   auto process = [&](int c4) -> float4 {
@@ -509,6 +519,8 @@ __global__ void __launch_bounds__(256) qkv_decode_finish_kernel(
     float* __restrict__ acc, int H, int C, __nv_bfloat16* __restrict__ q_out, int ld_q,
     __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc, const int* __restrict__ pos, int cap,
     const float* __restrict__ cos_t, const float* __restrict__ sin_t, int max_pos, float eps) {
+  pdl_trigger();
+  pdl_wait();
   const int m = blockIdx.x, warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int p = pos[m];
   const int pp = min(p, max_pos - 1);
@@ -598,17 +610,16 @@ void decode_attention(torch::Tensor qkv, torch::Tensor k_cache, torch::Tensor v_
   const at::cuda::CUDAGuard guard(qkv.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const float scale_log2 = float(kLog2e / std::sqrt(128.0));
-  decode_attn_kernel<<<dim3(S, H, B), kDecThreads, 0, st>>>(
-      reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), int(qkv.stride(0)),
-      reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr()),
-      reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr()), pos.data_ptr<int>(), int(H), cap, int(chunk),
-      scale_log2, part_o.data_ptr<float>(), part_ml.data_ptr<float>(),
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), int(out.stride(0)));
+  launch_k(decode_attn_kernel, dim3(S, H, B), dim3(kDecThreads), 0, st,
+           reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), int(qkv.stride(0)),
+           reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr()),
+           reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr()), pos.data_ptr<int>(), int(H), cap, int(chunk),
+           scale_log2, part_o.data_ptr<float>(), part_ml.data_ptr<float>(),
+           reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), int(out.stride(0)));
   if (S > 1)
-    decode_combine_kernel<<<dim3(H, B), 128, 0, st>>>(part_o.data_ptr<float>(), part_ml.data_ptr<float>(),
-                                                      pos.data_ptr<int>(), int(H), S, int(chunk), cap,
-                                                      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
-                                                      int(out.stride(0)));
+    launch_k(decode_combine_kernel, dim3(H, B), dim3(128), 0, st, part_o.data_ptr<float>(),
+             part_ml.data_ptr<float>(), pos.data_ptr<int>(), int(H), S, int(chunk), cap,
+             reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), int(out.stride(0)));
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "decode_attention launch failed");
 }
 
@@ -641,7 +652,7 @@ void sample_tokens(torch::Tensor logits, double temperature, int64_t top_k, torc
     smem_set = smem;
   }
   const at::cuda::CUDAGuard guard(logits.device());
-  sample_tokens_kernel<<<B, kSampThreads, smem, at::cuda::getCurrentCUDAStream()>>>(
+  launch_k(sample_tokens_kernel, dim3(B), dim3(kSampThreads), smem, at::cuda::getCurrentCUDAStream(),
       reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), int(logits.stride(0)), int(V), vpt,
       float(temperature), int(top_k), uniforms.data_ptr<double>(), int(B), int(max_steps), gen_count.data_ptr<int>(),
       out_tokens.data_ptr<int>(), next_in.data_ptr<int64_t>(), pos.data_ptr<int>(), advance_pos ? 1 : 0);
@@ -671,7 +682,7 @@ void skinny_finish(torch::Tensor acc, torch::Tensor out, int64_t mode, c10::opti
     TORCH_CHECK(N <= 4 * kFinThreads * kFinKeep, "skinny_finish: the fused norm takes N <= 2048");
   }
   const at::cuda::CUDAGuard guard(acc.device());
-  skinny_finish_kernel<<<M, kFinThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
+  launch_k(skinny_finish_kernel, dim3(M), dim3(kFinThreads), 0, at::cuda::getCurrentCUDAStream(),
       acc.data_ptr<float>(), int(N), int(mode), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
       int(out.stride(0)), mode == 3 ? reinterpret_cast<const __nv_bfloat16*>(aux->data_ptr()) : nullptr,
       mode == 3 ? int(aux->stride(0)) : 0,
@@ -698,7 +709,7 @@ void qkv_decode_finish(torch::Tensor acc, torch::Tensor qkv, torch::Tensor k_cac
   check_i32(pos, M, "qkv_decode_finish pos");
   TORCH_CHECK(cos_t.is_contiguous() && sin_t.is_contiguous() && cos_t.size(1) == 64, "qkv_decode_finish: tables");
   const at::cuda::CUDAGuard guard(acc.device());
-  qkv_decode_finish_kernel<<<M, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+  launch_k(qkv_decode_finish_kernel, dim3(M), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
       acc.data_ptr<float>(), int(H), int(C), reinterpret_cast<__nv_bfloat16*>(qkv.data_ptr()), int(qkv.stride(0)),
       reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()), reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()),
       pos.data_ptr<int>(), int(k_cache.size(2)), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),

@@ -20,6 +20,8 @@
 //
 // Warps: 0 = TMA/bulk loads, 1 = TMEM allocation + MMA issue, 2-5 = compute,
 // 6-9 = dQ drain. Every wait is bounded (common.cuh).
+#include <cstdlib>
+
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -32,10 +34,11 @@ namespace nk {
 
 namespace fb {
 constexpr int HD = 128, BK = 128, BQ = 128;
-constexpr int kThreads = 320;
+constexpr int kThreads = 448;  // 2 + 8 compute + 4 drain warps
 constexpr int kTile = 128 * 128 * 2;   // 32 KB
 constexpr int kSub = 128 * 64 * 2;     // 16 KB swizzle sub-tile
-constexpr int kSmem = 6 * kTile + 2 * BQ * 4 + 1024 + 256;
+constexpr int kStage = 32 * 32 * 4;  // 4 KB: one drain warp's 32 x 32 fp32 dQ chunk
+constexpr int kSmem = 6 * kTile + 4 * 2 * kStage + 2 * BQ * 4 + 1024 + 256;
 }  // namespace fb
 
 struct FbArgs {
@@ -53,6 +56,7 @@ struct FbArgs {
   const float* rope_rstd;
   const float* rope_cos;
   const float* rope_sin;
+  int dbg;
 };
 
 __device__ __forceinline__ uint32_t tile_off(int r, int c) {  // 16B chunk c (of 16) in row r, K-major SW128
@@ -61,7 +65,7 @@ __device__ __forceinline__ uint32_t tile_off(int r, int c) {  // 16B chunk c (of
 
 __global__ void __launch_bounds__(fb::kThreads, 1)
     flash_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tmo,
-                        const FbArgs a) {
+                        const __grid_constant__ CUtensorMap tmq, const FbArgs a) {
   using namespace fb;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -71,9 +75,10 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
   uint8_t* sO = smem + 3 * kTile;   // dO_j
   uint8_t* sP = smem + 4 * kTile;   // P^T  [key][query]
   uint8_t* sS = smem + 5 * kTile;   // dS^T [key][query]
-  float* sL = reinterpret_cast<float*>(smem + 6 * kTile);  // lse2 of the query block
+  uint8_t* sStage = smem + 6 * kTile;  // drain warps: 2 x 4 KB each (dQ chunks for TMA reduce-add)
+  float* sL = reinterpret_cast<float*>(smem + 6 * kTile + 8 * kStage);  // lse2 of the query block
   float* sD = sL + BQ;                                     // D of the query block
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTile + 2 * BQ * 4);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTile + 8 * kStage + 2 * BQ * 4);
   uint64_t* kv_full = bars + 0;
   uint64_t* qd_full = bars + 1;
   uint64_t* qd_empty = bars + 2;
@@ -96,7 +101,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
     mbar_init(qd_full, 1);
     mbar_init(qd_empty, 1);
     mbar_init(st_full, 1);
-    mbar_init(p_full, 4);
+    mbar_init(p_full, 8);
     mbar_init(dq_full, 1);
     mbar_init(dq_free, 4);
     mbar_init(kv_done, 1);
@@ -175,44 +180,57 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       }
       umma_commit(kv_done);
     }
-  } else if (warp < 6) {
-    // Compute warpgroup: thread = key row.
+  } else if (warp < 10) {
+    // Compute warps: thread = key row; two warps per TMEM lane quarter, each
+    // taking 64 of the block's 128 query columns.
     const int quarter = warp & 3;
+    const int half = (warp - 2) / 4;
     const int r = quarter * 32 + lane;
     const int key = kb * BK + r;
     const uint32_t lanes = uint32_t(quarter * 32) << 16;
     bool ok = true;
+    // P^T and dS^T for 32 query columns starting at c * 32.
+    auto chunk = [&](int c, int j, bool diag) {
+      float s[32], dp[32];
+      tmem_ld_32x32(tmem + lanes + c * 32, s);
+      tmem_ld_32x32(tmem + lanes + 128 + c * 32, dp);
+      uint32_t pp[16], dd[16];
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        const float4 l4 = *reinterpret_cast<const float4*>(sL + c * 32 + i);
+        const float4 d4 = *reinterpret_cast<const float4*>(sD + c * 32 + i);
+        const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
+        float pv[4], gv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (a.dbg & 2) { pv[e] = s[i + e]; gv[e] = dp[i + e]; continue; }
+          pv[e] = exp2f(fmaf(s[i + e], a.sl2, -lv[e]));
+          if (diag && (j * BQ + c * 32 + i + e) < key) pv[e] = 0.f;
+          gv[e] = pv[e] * (dp[i + e] - dv4[e]);
+        }
+        pp[i / 2] = pack_bf16x2(pv[0], pv[1]);
+        pp[i / 2 + 1] = pack_bf16x2(pv[2], pv[3]);
+        dd[i / 2] = pack_bf16x2(gv[0], gv[1]);
+        dd[i / 2 + 1] = pack_bf16x2(gv[2], gv[3]);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        *reinterpret_cast<uint4*>(sP + tile_off(r, c * 4 + u)) = make_uint4(pp[4 * u], pp[4 * u + 1], pp[4 * u + 2], pp[4 * u + 3]);
+        *reinterpret_cast<uint4*>(sS + tile_off(r, c * 4 + u)) = make_uint4(dd[4 * u], dd[4 * u + 1], dd[4 * u + 2], dd[4 * u + 3]);
+      }
+    };
     for (int n = 0; n < nblk && ok; ++n) {
       const int j = kb + n;
       if (!mbar_wait(st_full, n & 1, kErrTimeoutEpilogue, a.err)) { ok = false; break; }
       tc_fence_after();
       // P^T / dS^T tiles are free once the previous block's MMAs finished.
       if (n > 0 && !mbar_wait(qd_empty, (n - 1) & 1, kErrTimeoutEpilogue, a.err)) { ok = false; break; }
-      const bool diag = n == 0;
-#pragma unroll 1
-      for (int c = 0; c < BQ / 32; ++c) {
-        float s[32], dp[32];
-        tmem_ld_32x32(tmem + lanes + c * 32, s);
-        tmem_ld_32x32(tmem + lanes + 128 + c * 32, dp);
-        uint32_t pp[16], dd[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float pv[2], dv[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int qi = c * 32 + i + e;
-            const bool masked = diag && (j * BQ + qi) < key;
-            pv[e] = masked ? 0.f : exp2f(s[i + e] * a.sl2 - sL[qi]);
-            dv[e] = pv[e] * (dp[i + e] - sD[qi]);
-          }
-          pp[i / 2] = pack_bf16x2(pv[0], pv[1]);
-          dd[i / 2] = pack_bf16x2(dv[0], dv[1]);
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          *reinterpret_cast<uint4*>(sP + tile_off(r, c * 4 + u)) = make_uint4(pp[4 * u], pp[4 * u + 1], pp[4 * u + 2], pp[4 * u + 3]);
-          *reinterpret_cast<uint4*>(sS + tile_off(r, c * 4 + u)) = make_uint4(dd[4 * u], dd[4 * u + 1], dd[4 * u + 2], dd[4 * u + 3]);
-        }
+      if (n == 0) {  // the diagonal block: causal mask
+        chunk(2 * half, j, true);
+        chunk(2 * half + 1, j, true);
+      } else {
+        chunk(2 * half, j, false);
+        chunk(2 * half + 1, j, false);
       }
       fence_proxy_async();
       tc_fence_before();
@@ -221,9 +239,8 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
     }
     if (ok && mbar_wait(kv_done, 0, kErrTimeoutEpilogue, a.err)) {
       tc_fence_after();
-      if (key < a.T) {
-        __nv_bfloat16* dk = a.dqkv + (long(b) * a.T + key) * 3 * a.C + a.C + h * HD;
-        __nv_bfloat16* dv = dk + a.C;
+      if (key < a.T && half == 1) {
+        __nv_bfloat16* dv = a.dqkv + (long(b) * a.T + key) * 3 * a.C + 2 * a.C + h * HD;
 #pragma unroll 1
         for (int c = 0; c < HD / 32; ++c) {
           float y[32];
@@ -234,75 +251,105 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
                 pack_bf16x2(y[8 * u], y[8 * u + 1]), pack_bf16x2(y[8 * u + 2], y[8 * u + 3]),
                 pack_bf16x2(y[8 * u + 4], y[8 * u + 5]), pack_bf16x2(y[8 * u + 6], y[8 * u + 7]));
         }
-        float g[HD];
-#pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
-          float x[32];
-          tmem_ld_32x32(tmem + lanes + 256 + c * 32, x);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) g[c * 32 + i] = x[i] * a.scale;
-        }
+      } else if (key < a.T) {
+        __nv_bfloat16* dk = a.dqkv + (long(b) * a.T + key) * 3 * a.C + a.C + h * HD;
+        // dK = scale * acc; with the RoPE fold, d/dx of y = rms(rope(x)):
+        // dr = r (g - y <g, y> / D), then the transposed rotation of the
+        // pairs (i, i + 64). Columns are processed 32 + 32 at a time.
+        const long row = long(b) * a.T + key;
+        const __nv_bfloat16* yk = a.qkv + row * 3 * a.C + a.C + h * HD;
+        float dot = 0.f, r = 0.f;
         if (a.rope_rstd) {
-          // d/dx of y = rms(rope(x)): dr = r (g - y <g, y> / D), then the transposed rotation.
-          const long row = long(b) * a.T + key;
-          const __nv_bfloat16* yk = a.qkv + row * 3 * a.C + a.C + h * HD;
-          const float r = a.rope_rstd[row * 2 * a.H + a.H + h];
-          float dot = 0.f;
+          r = a.rope_rstd[row * 2 * a.H + a.H + h];
+#pragma unroll 1
+          for (int c = 0; c < HD / 32; ++c) {
+            float x[32];
+            tmem_ld_32x32(tmem + lanes + 256 + c * 32, x);
 #pragma unroll
-          for (int i = 0; i < HD; i += 2) {
-            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(yk + i));
-            dot += f.x * g[i] + f.y * g[i + 1];
+            for (int i = 0; i < 32; i += 2) {
+              const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(yk + c * 32 + i));
+              dot += f.x * x[i] + f.y * x[i + 1];
+            }
           }
-          dot /= float(HD);
-          const float* cr = a.rope_cos + long(key) * 64;
-          const float* sr = a.rope_sin + long(key) * 64;
+          dot *= a.scale / float(HD);
+        }
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          float x1[32], x2[32];
+          tmem_ld_32x32(tmem + lanes + 256 + c * 32, x1);
+          tmem_ld_32x32(tmem + lanes + 256 + (c + 2) * 32, x2);
 #pragma unroll
-          for (int i = 0; i < 64; ++i) {
-            const float y1 = __bfloat162float(yk[i]), y2 = __bfloat162float(yk[i + 64]);
-            const float d1 = r * (g[i] - y1 * dot), d2 = r * (g[i + 64] - y2 * dot);
-            const float cs = __ldg(cr + i), sn = __ldg(sr + i);
-            g[i] = d1 * cs - d2 * sn;       // dx1 = dy1 cos - dy2 sin
-            g[i + 64] = d1 * sn + d2 * cs;  // dx2 = dy1 sin + dy2 cos
+          for (int i = 0; i < 32; ++i) {
+            float g1 = x1[i] * a.scale, g2 = x2[i] * a.scale;
+            if (a.rope_rstd) {
+              const int col = c * 32 + i;
+              const float y1 = __bfloat162float(yk[col]), y2 = __bfloat162float(yk[col + 64]);
+              const float d1 = r * (g1 - y1 * dot), d2 = r * (g2 - y2 * dot);
+              const float cs = __ldg(a.rope_cos + long(key) * 64 + col), sn = __ldg(a.rope_sin + long(key) * 64 + col);
+              g1 = d1 * cs - d2 * sn;  // dx1 = dy1 cos - dy2 sin
+              g2 = d1 * sn + d2 * cs;  // dx2 = dy1 sin + dy2 cos
+            }
+            x1[i] = g1;
+            x2[i] = g2;
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            *reinterpret_cast<uint4*>(dk + c * 32 + u * 8) =
+                make_uint4(pack_bf16x2(x1[8 * u], x1[8 * u + 1]), pack_bf16x2(x1[8 * u + 2], x1[8 * u + 3]),
+                           pack_bf16x2(x1[8 * u + 4], x1[8 * u + 5]), pack_bf16x2(x1[8 * u + 6], x1[8 * u + 7]));
+            *reinterpret_cast<uint4*>(dk + 64 + c * 32 + u * 8) =
+                make_uint4(pack_bf16x2(x2[8 * u], x2[8 * u + 1]), pack_bf16x2(x2[8 * u + 2], x2[8 * u + 3]),
+                           pack_bf16x2(x2[8 * u + 4], x2[8 * u + 5]), pack_bf16x2(x2[8 * u + 6], x2[8 * u + 7]));
           }
         }
-#pragma unroll
-        for (int u = 0; u < HD / 8; ++u)
-          *reinterpret_cast<uint4*>(dk + u * 8) =
-              make_uint4(pack_bf16x2(g[8 * u], g[8 * u + 1]), pack_bf16x2(g[8 * u + 2], g[8 * u + 3]),
-                         pack_bf16x2(g[8 * u + 4], g[8 * u + 5]), pack_bf16x2(g[8 * u + 6], g[8 * u + 7]));
       } else {
         // Lanes past the sequence still take part in the warp-collective loads.
 #pragma unroll 1
         for (int c = 0; c < HD / 32; ++c) {
           float x[32];
-          tmem_ld_32x32(tmem + lanes + 256 + c * 32, x);
-          tmem_ld_32x32(tmem + lanes + 384 + c * 32, x);
+          tmem_ld_32x32(tmem + lanes + (half ? 384 : 256) + c * 32, x);
         }
       }
     }
   } else {
-    // dQ drain warpgroup: thread = query row of the current block.
+    // dQ drain warps: thread = query row of the current block. Each warp
+    // stages 32 rows x 32 columns of dQ * scale (fp32, 128B-swizzled) and
+    // adds them to the fp32 accumulator with one TMA reduce-add; two staging
+    // buffers per warp let the next chunk fill while the previous one drains.
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;
     const uint32_t lanes = uint32_t(quarter * 32) << 16;
+    uint8_t* stage = sStage + (warp - 10) * 2 * kStage;
+    int chunks = 0;
     for (int n = 0; n < nblk; ++n) {
       const int j = kb + n;
       if (!mbar_wait(dq_full, n & 1, kErrTimeoutEpilogue, a.err)) break;
       tc_fence_after();
-      float* dst = a.dq_acc + (long(b) * a.T + j * BQ + r) * a.C + h * HD;
 #pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
+      for (int c = 0; c < HD / 32; ++c, ++chunks) {
         float x[32];
         tmem_ld_32x32(tmem + lanes + 128 + c * 32, x);
+        if (a.dbg & 1) continue;
+        uint8_t* buf = stage + (chunks & 1) * kStage;
+        if (lane == 0 && chunks >= 2) bulk_wait_read<1>();  // this buffer's previous reduce has read it
+        __syncwarp();
 #pragma unroll
-        for (int u = 0; u < 32; u += 4)
-          atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + u),
-                    make_float4(x[u] * a.scale, x[u + 1] * a.scale, x[u + 2] * a.scale, x[u + 3] * a.scale));
+        for (int k = 0; k < 8; ++k)
+          *reinterpret_cast<float4*>(buf + lane * 128 + ((k ^ (lane & 7)) << 4)) =
+              make_float4(x[4 * k] * a.scale, x[4 * k + 1] * a.scale, x[4 * k + 2] * a.scale, x[4 * k + 3] * a.scale);
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];"
+                       ::"l"(&tmq), "r"(smem_u32(buf)), "r"(h * HD + c * 32), "r"(b * a.T + j * BQ + quarter * 32)
+                       : "memory");
+          bulk_commit();
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_free);
     }
+    if (lane == 0) bulk_wait<0>();
   }
   tc_fence_before();
   __syncthreads();
@@ -394,6 +441,18 @@ void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torc
               "flash_bwd_tc: memset");
   CUtensorMap tm = seq_map_3d(qkv.data_ptr(), B, T, 3 * C);
   CUtensorMap tmo = seq_map_3d(dout.data_ptr(), B, T, C);
+  CUtensorMap tmq;
+  {
+    cuuint64_t dims[2] = {cuuint64_t(C), cuuint64_t(B * T)};
+    cuuint64_t strides[1] = {cuuint64_t(C * 4)};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(dq_acc.data_ptr()) % 16 == 0, "flash_bwd_tc: dq_acc alignment");
+    CUresult r = encode_tiled_fn()(&tmq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dq_acc.data_ptr(), dims, strides, box,
+                                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    TORCH_CHECK(r == CUDA_SUCCESS, "flash_bwd_tc: dq tensor map encode failed ", int(r));
+  }
   FbArgs a{};
   a.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
   a.dq_acc = dq_acc.data_ptr<float>();
@@ -403,6 +462,7 @@ void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torc
   a.scale = 1.f / std::sqrt(float(HD));
   a.sl2 = a.scale * 1.4426950408889634f;
   a.err = error_word();
+  if (const char* d = std::getenv("NANOGPT_FB_DEBUG")) a.dbg = std::atoi(d);
   if (rope_rstd.has_value()) {
     TORCH_CHECK(rope_cos.has_value() && rope_sin.has_value() && rope_cos->size(1) == 64 && rope_cos->size(0) >= T,
                 "flash_bwd_tc: rope tables");
@@ -418,7 +478,7 @@ void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torc
     configured = true;
   }
   dim3 grid(unsigned(T / BK), unsigned(B * H));
-  flash_bwd_tc_kernel<<<grid, kThreads, kSmem, stream>>>(tm, tmo, a);
+  flash_bwd_tc_kernel<<<grid, kThreads, kSmem, stream>>>(tm, tmo, tmq, a);
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "flash_bwd_tc launch failed");
   const long items = B * T * H;
   dq_finish_kernel<<<unsigned((items + 7) / 8), 256, 0, stream>>>(a.dq_acc, a.dqkv, B * T, int(T), int(H), int(C),

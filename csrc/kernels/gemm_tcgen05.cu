@@ -23,6 +23,9 @@
 
 #include "common.cuh"
 #include "status.h"
+#include <cstdlib>
+
+#include "launch.h"
 #include "tma_host.h"
 
 namespace nk {
@@ -58,16 +61,20 @@ struct GemmArgs {
   float* rope_rstd;
   int rope_T, rope_H, rope_C;
   float rope_eps;
+  // A (K-major) depends on no earlier kernel (a weight): under programmatic
+  // dependent launch its first tiles are fetched before griddepcontrol.wait.
+  int a_independent;
 };
 
 constexpr int BM = 128, BK = 64, kGroupM = 16;
 constexpr int kEpiWarps = 8, kThreads = 64 + 32 * kEpiWarps;
 
-template <int BN>
+template <int BN, bool PAIR>
 struct Smem {
-  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kBRows = PAIR ? BN / 2 : BN;  // B rows this CTA holds (a pair splits N)
+  static constexpr int kStages = (PAIR || BN == 128) ? 6 : 4;
   static constexpr int kABytes = BM * BK * 2;
-  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kBBytes = kBRows * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTotal = kStages * kStageBytes + kEpiWarps * 2 * 2048 /*epilogue staging*/ +
                                 1024 /*align*/ + 512 /*barriers*/;
@@ -144,12 +151,22 @@ __device__ __forceinline__ void atomic_chunk_t(const GemmArgs& a, int row, int c
     if (col0 + i < a.N) atomicAdd(c + long(col0 + i) * a.ldc, a.alpha * v[i]);
 }
 
-template <int BN>
+// PAIR: a cluster of two CTAs computes a 256 x BN tile with cta_group::2
+// MMAs. Each CTA loads its own 128 rows of A and BN/2 rows of B (no
+// multicast); the leader (rank 0) issues the MMAs, which read both CTAs'
+// shared memory and accumulate each CTA's 128 rows in its own tensor memory.
+// Both CTAs' TMA bytes are counted on the leader's full barrier; the leader's
+// MMA completion is committed to both CTAs' empty / accumulator-full
+// barriers; both CTAs' epilogue warps arrive on the leader's accumulator-empty
+// barrier. Per 256 x BN x 64 step the pair moves 64 KB from L2 instead of the
+// 96 KB two independent 128 x BN tiles would.
+template <int BN, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX,
                      const GemmArgs args) {
-  using S = Smem<BN>;
+  using S = Smem<BN, PAIR>;
+  constexpr int kTileM = PAIR ? 2 * BM : BM;
   constexpr int STAGES = S::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -163,18 +180,30 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int units = args.num_m * args.num_n * args.splits;
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
+  const bool leader = rank == 0;
+  const int cta_id = PAIR ? int(blockIdx.x) / 2 : int(blockIdx.x);
+  const int n_ctas = PAIR ? int(gridDim.x) / 2 : int(gridDim.x);
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
-    for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], kEpiWarps); }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], PAIR ? 2 * kEpiWarps : kEpiWarps);
+    }
     for (int w = 0; w < kEpiWarps; ++w) mbar_init(&aux_bar[w], 1);
     fence_barrier_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
   }
-  if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
+  if (warp == 1) {
+    if (PAIR) tmem_alloc_pair(tmem_slot, 2 * BN);
+    else tmem_alloc(tmem_slot, 2 * BN);
+  }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync();  // the peer's barriers exist before any cross-CTA arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -183,38 +212,66 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      // Weight tiles of the first stages go out before the dependency wait.
+      int pre = 0;
+      if (!PAIR && args.a_independent && !args.a_mn_major && int(blockIdx.x) < units) {
+        int m, n, kb0, kb1;
+        unit_coords(args, blockIdx.x, m, n, kb0, kb1);
+        for (int kb = kb0; kb < kb1 && pre < STAGES; ++kb, ++pre) {
+          mbar_arrive_expect_tx(&full_bar[pre], S::kStageBytes);
+          tma_load_2d(smem + pre * S::kStageBytes, &tmA, &full_bar[pre], kb * BK, m * BM);
+        }
+      }
+      pdl_wait();
+      auto load = [&](void* dst, const CUtensorMap* map, int stage_, int c0, int c1) {
+        if (PAIR) tma_load_2d_pair(dst, map, map_to_cta(&full_bar[stage_], 0), c0, c1);
+        else tma_load_2d(dst, map, &full_bar[stage_], c0, c1);
+      };
+      int issued = 0;
+      for (int u = cta_id; u < units && ok; u += n_ctas) {
         int m, n, kb0, kb1;
         unit_coords(args, u, m, n, kb0, kb1);
-        for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&empty_bar[stage], phase ^ 1, kErrTimeoutProducer, args.err)) { ok = false; break; }
+        const int arow = m * kTileM + int(rank) * BM;        // this CTA's 128 rows of A
+        const int brow = n * BN + int(rank) * S::kBRows;     // and its rows of B
+        for (int kb = kb0; kb < kb1; ++kb, ++issued) {
           uint8_t* sa = smem + stage * S::kStageBytes;
           uint8_t* sb = sa + S::kABytes;
-          mbar_arrive_expect_tx(&full_bar[stage], S::kStageBytes);
-          if (!args.a_mn_major) {
-            tma_load_2d(sa, &tmA, &full_bar[stage], kb * BK, m * BM);
-          } else {
+          if (issued >= pre) {
+            if (!mbar_wait(&empty_bar[stage], phase ^ 1, kErrTimeoutProducer, args.err)) { ok = false; break; }
+            if (leader) mbar_arrive_expect_tx(&full_bar[stage], (PAIR ? 2 : 1) * S::kStageBytes);
+            if (!args.a_mn_major) {
+              load(sa, &tmA, stage, kb * BK, arow);
+            } else {
 #pragma unroll
-            for (int j = 0; j < BM / 64; ++j) tma_load_2d(sa + j * 8192, &tmA, &full_bar[stage], m * BM + 64 * j, kb * BK);
+              for (int j = 0; j < BM / 64; ++j) load(sa + j * 8192, &tmA, stage, arow + 64 * j, kb * BK);
+            }
           }
           if (!args.b_mn_major) {
-            tma_load_2d(sb, &tmB, &full_bar[stage], kb * BK, n * BN);
+            load(sb, &tmB, stage, kb * BK, brow);
           } else {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 8192, &tmB, &full_bar[stage], n * BN + 64 * j, kb * BK);
+            for (int j = 0; j < S::kBRows / 64; ++j) load(sb + j * 8192, &tmB, stage, brow + 64 * j, kb * BK);
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = idesc_bf16(BM, BN, args.a_mn_major, args.b_mn_major);
+    if (lane == 0 && leader) {
+      const uint32_t idesc = idesc_bf16(kTileM, BN, args.a_mn_major, args.b_mn_major);
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++local) {
+      auto commit = [&](uint64_t* bar) {
+        if (PAIR) {
+          umma_commit_pair(map_to_cta(bar, 0));
+          umma_commit_pair(map_to_cta(bar, 1));
+        } else {
+          umma_commit(bar);
+        }
+      };
+      for (int u = cta_id; u < units && ok; u += n_ctas, ++local) {
         int m, n, kb0, kb1;
         unit_coords(args, u, m, n, kb0, kb1);
         const int b = local & 1;
@@ -233,15 +290,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                 : sw128_desc(sa + k * 32, 16, 1024);
             const uint64_t bd = args.b_mn_major ? sw128_desc(sb + k * 2048, 8192, 1024)
                                                 : sw128_desc(sb + k * 32, 16, 1024);
-            umma_bf16(d_tmem, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+            if (PAIR) umma_bf16_pair(d_tmem, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+            else umma_bf16(d_tmem, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
-          umma_commit(&empty_bar[stage]);
+          commit(&empty_bar[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
-        umma_commit(&acc_full[b]);
+        commit(&acc_full[b]);
       }
     }
   } else {
+    pdl_wait();                             // the epilogue reads and writes global memory
     const int ew = warp - 2;                // epilogue warp index
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
     const int half = ew / 4;                // which half of the tile's columns
@@ -252,14 +311,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t aux_phase = 0;
     bool ok = true;
     int local = 0;
-    for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++local) {
+    auto release_acc = [&](int b) {
+      if (PAIR) mbar_arrive_cluster(map_to_cta(&acc_empty[b], 0));
+      else mbar_arrive(&acc_empty[b]);
+    };
+    for (int u = cta_id; u < units && ok; u += n_ctas, ++local) {
       int m, n, kb0, kb1;
       unit_coords(args, u, m, n, kb0, kb1);
       const int b = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&acc_full[b], acc_phase, kErrTimeoutEpilogue, args.err)) break;
       tc_fence_after();
-      const int row0 = m * BM + q * 32;
+      const int row0 = m * kTileM + int(rank) * BM + q * 32;
       if (args.mode == kRopeNorm && n * BN + half * 128 < 2 * args.rope_C) {
         // One full q/k head per thread row: 4 TMEM chunks -> RoPE -> RMSNorm -> 4 TMA stores.
         const int colb = n * BN + half * 128;
@@ -305,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[b]);
+        if (lane == 0) release_acc(b);
         continue;
       }
 #pragma unroll 1
@@ -363,15 +426,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      if (lane == 0) release_acc(b);
     }
     if (lane == 0) bulk_wait<0>();
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync();  // no cross-CTA MMA, TMA byte count or arrive is still in flight
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 2 * BN);
+    if (PAIR) tmem_dealloc_pair(tmem_base, 2 * BN);
+    else tmem_dealloc(tmem_base, 2 * BN);
   }
 }
 
@@ -385,20 +450,53 @@ static int num_sms() {
   return n;
 }
 
-template <int BN>
+template <int BN, bool PAIR>
 static void launch(const GemmArgs& args, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                    const CUtensorMap& tx, cudaStream_t stream) {
+  using S = Smem<BN, PAIR>;
   static bool configured = false;
   if (!configured) {
-    TORCH_CHECK(cudaFuncSetAttribute(gemm_bf16_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     Smem<BN>::kTotal) == cudaSuccess,
+    TORCH_CHECK(cudaFuncSetAttribute(gemm_bf16_kernel<BN, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     S::kTotal) == cudaSuccess,
                 "gemm: cannot reserve shared memory");
     configured = true;
   }
   const int units = args.num_m * args.num_n * args.splits;
-  const int grid = std::min(units, num_sms());
-  gemm_bf16_kernel<BN><<<grid, kThreads, Smem<BN>::kTotal, stream>>>(ta, tb, tc, tx, args);
+  if constexpr (!PAIR) {
+    const int grid = std::min(units, num_sms());
+    TORCH_CHECK(launch_k(gemm_bf16_kernel<BN, false>, dim3(grid), dim3(kThreads), S::kTotal, stream, ta, tb, tc,
+                         tx, args) == cudaSuccess,
+                "gemm: launch failed");
+  } else {
+    const int grid = 2 * std::min(units, num_sms() / 2);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = S::kTotal;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    TORCH_CHECK(cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<BN, true>, ta, tb, tc, tx, args) == cudaSuccess,
+                "gemm: pair launch failed");
+  }
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "gemm launch failed");
+}
+
+// CTA pairs (cta_group::2) for the large 256-column GEMMs; NANOGPT_GEMM_PAIR=0
+// selects single-CTA tiles everywhere.
+static bool pair_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("NANOGPT_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 static void check_bf16_2d(const torch::Tensor& t, int64_t rows, int64_t cols, const char* what) {
@@ -412,7 +510,7 @@ static void check_bf16_2d(const torch::Tensor& t, int64_t rows, int64_t cols, co
 //   A: a_mn_major ? [K, M] : [M, K]      B: b_mn_major ? [K, N] : [N, K]
 void gemm_impl(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_major, torch::Tensor C, int64_t mode,
                double alpha, c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> aux_out, int64_t splits,
-               int64_t block_n, const GemmArgs* rope) {
+               int64_t block_n, const GemmArgs* rope, bool a_independent = false) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda(), "gemm: CUDA tensors required");
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm: bf16 operands");
   TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "gemm: 2-D tensors");
@@ -440,6 +538,7 @@ void gemm_impl(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_majo
   args.C = C.data_ptr();
   args.ldc = C.stride(0);
   args.err = error_word();
+  args.a_independent = a_independent ? 1 : 0;
   if (rope) {
     args.rope_cos = rope->rope_cos; args.rope_sin = rope->rope_sin; args.rope_rstd = rope->rope_rstd;
     args.rope_T = rope->rope_T; args.rope_H = rope->rope_H; args.rope_C = rope->rope_C; args.rope_eps = rope->rope_eps;
@@ -457,7 +556,11 @@ void gemm_impl(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_majo
     args.ld_aux_out = aux_out->stride(0);
   }
   const int BN = block_n == 128 ? 128 : 256;
-  args.num_m = (M + BM - 1) / BM;
+  // Pairs measured faster than single-CTA tiles only for the weight-gradient
+  // products (both operands MN-major); elsewhere single-CTA tiles win.
+  const bool pair = BN == 256 && M > BM && a_mn_major && b_mn_major && mode != kRopeNorm && mode != kAtomicF32T &&
+                    pair_enabled();
+  args.num_m = (M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM);
   args.num_n = (N + BN - 1) / BN;
   args.kb_total = (K + BK - 1) / BK;
   int s = int(std::max<int64_t>(1, std::min<int64_t>(splits, args.kb_total)));
@@ -469,7 +572,7 @@ void gemm_impl(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_majo
   CUtensorMap ta = a_mn_major ? make_tmap_bf16_2d(A.data_ptr(), M, K, A.stride(0), 64, 64)
                               : make_tmap_bf16_2d(A.data_ptr(), K, M, A.stride(0), 64, BM);
   CUtensorMap tb = b_mn_major ? make_tmap_bf16_2d(B.data_ptr(), N, K, B.stride(0), 64, 64)
-                              : make_tmap_bf16_2d(B.data_ptr(), K, N, B.stride(0), 64, BN);
+                              : make_tmap_bf16_2d(B.data_ptr(), K, N, B.stride(0), 64, pair ? BN / 2 : BN);
   // Epilogue maps: 32 x 32 bf16 boxes, 64-byte swizzle (unused in the fp32 atomic mode).
   CUtensorMap tc = ta, tx = ta;
   if (!f32out) {
@@ -481,8 +584,9 @@ void gemm_impl(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_majo
   }
   const at::cuda::CUDAGuard guard(A.device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  if (BN == 128) launch<128>(args, ta, tb, tc, tx, stream);
-  else launch<256>(args, ta, tb, tc, tx, stream);
+  if (BN == 128) launch<128, false>(args, ta, tb, tc, tx, stream);
+  else if (pair) launch<256, true>(args, ta, tb, tc, tx, stream);
+  else launch<256, false>(args, ta, tb, tc, tx, stream);
 }
 
 void gemm(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_major, torch::Tensor C, int64_t mode,
@@ -509,4 +613,13 @@ void gemm_qkv_rope(torch::Tensor x, torch::Tensor w, torch::Tensor qkv, torch::T
   gemm_impl(x, false, w, false, qkv, kRopeNorm, 1.0, c10::nullopt, c10::nullopt, 1, 256, &r);
 }
 
+}  // namespace nk
+
+namespace nk {
+// acc[M, N] (fp32) += x[M, K] . w[N, K]^T with the operands swapped (the weight
+// rows are the 128-row tile side), split over K, transposed fp32 atomics. The
+// weight tiles are independent of earlier kernels (prefetched under PDL).
+void gemm_skinny_acc(torch::Tensor w, torch::Tensor x, torch::Tensor acc, int64_t splits) {
+  gemm_impl(w, false, x, false, acc, kAtomicF32T, 1.0, c10::nullopt, c10::nullopt, splits, 128, nullptr, true);
+}
 }  // namespace nk

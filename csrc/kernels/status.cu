@@ -24,4 +24,8 @@ int64_t kernel_status(bool reset) {
   return v;
 }
 
+static bool g_pdl = false;
+bool pdl_enabled() { return g_pdl; }
+void set_pdl(bool on) { g_pdl = on; }
+
 }  // namespace nk

@@ -33,6 +33,7 @@ def main(argv=None):
     p.add_argument("--batch", type=int, default=64)
     p.add_argument("--ctx", type=int, default=700)
     p.add_argument("--iters", type=int, default=50)
+    p.add_argument("--pdl", type=int, default=0, help="programmatic dependent launch in the decode chain (0/1)")
     a = p.parse_args(argv)
     from ..config import d_model
     from ..models.decode import DecodeEngine, draw_uniforms
@@ -47,6 +48,7 @@ def main(argv=None):
     init_params(store, seed=0, mode="bench")
     store.refresh_work()
     eng = DecodeEngine(store, a.batch, a.ctx + 64)
+    eng.pdl = bool(a.pdl)
     eng.k_cache.normal_()
     eng.v_cache.normal_()
     eng.pos.fill_(a.ctx)

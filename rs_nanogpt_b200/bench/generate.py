@@ -37,6 +37,7 @@ def main(argv=None):
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--repeats", type=int, default=3)
     p.add_argument("--no-graph", action="store_true")
+    p.add_argument("--pdl", type=int, default=0, help="programmatic dependent launch in the decode chain (0/1)")
     a = p.parse_args(argv)
 
     dev = torch.device("cuda", 0)
@@ -50,6 +51,7 @@ def main(argv=None):
                for _ in range(a.prompts)]
     cap = (max(map(len, prompts)) + 255) // 256 * 256 + a.new
     engine = DecodeEngine(store, a.prompts, cap)
+    engine.pdl = bool(a.pdl)
     generate_batch(engine, prompts, a.new, a.temperature, a.top_k, a.seed, use_graph=not a.no_graph)  # warm-up
     ttft, tps = [], []
     l0 = launch_count()
@@ -65,7 +67,7 @@ def main(argv=None):
         "metric": "KV-cache generation, d20 random-init bf16", "p50_ttft_ms": statistics.median(ttft),
         "decode_tokens_per_s": statistics.median(tps), "ttft_ms_runs": ttft, "decode_tok_s_runs": tps,
         "prompts": a.prompts, "prompt_tokens": sum(map(len, prompts)), "new_tokens": a.new,
-        "temperature": a.temperature, "top_k": a.top_k, "cuda_graph": not a.no_graph,
+        "temperature": a.temperature, "top_k": a.top_k, "cuda_graph": not a.no_graph, "pdl": bool(a.pdl),
         "host_launch_calls": (launch_count() - l0) // a.repeats,
         "clocks": clocks.summary(), "kernel_status": kernel_status(),
         "config": {"model": f"GPT d{a.depth}", "vocab": cfg.vocab_size, "kv_capacity": cap},

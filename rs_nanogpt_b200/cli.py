@@ -130,8 +130,9 @@ def build_parser() -> argparse.ArgumentParser:
 
 def _add_extensions(p: argparse.ArgumentParser) -> None:
     """Flags this framework adds on top of the reference's set."""
-    p.add_argument("--backend", choices=["nccl", "fused"], default="nccl",
-                   help="data-parallel gradient path: NCCL all-reduce (baseline) or the fused kernel")
+    p.add_argument("--backend", choices=["nccl", "fused"], default="fused",
+                   help="data-parallel gradient path on GPUs: the fused P2P reduce-scatter + AdamW + all-gather "
+                        "kernel (default) or the NCCL all-reduce baseline; CPU runs always use the gloo all-reduce")
     p.add_argument("--device", default=None, help="cuda or cpu (default: cuda when available)")
     p.add_argument("--init", choices=["reference", "bench"], default="reference",
                    help="weight init (pretrain only): the reference's, or N(0,0.02) with zero projections")

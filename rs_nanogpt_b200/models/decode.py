@@ -32,6 +32,7 @@ import torch
 
 from ..ops import gemm
 from ..ops import layers as L
+from ..ops._ext import ext
 from .fused import FusedGpt
 from .params import ParamStore
 
@@ -73,6 +74,7 @@ class DecodeEngine:
         self.out_tokens = None
         self.uniforms = None
         self._graph = None
+        self.pdl = False  # measured slower in the captured decode step (see the decode_step benchmark)
 
     # ---- prefill -------------------------------------------------------------------
 
@@ -104,7 +106,17 @@ class DecodeEngine:
     def step(self) -> torch.Tensor:
         """Feed ``next_in`` (one token per sequence) at position ``pos``;
         returns the (B, V) bf16 logits. ``pos`` is advanced by ``sample`` (or
-        by the caller when sampling on the host)."""
+        by the caller when sampling on the host). With ``self.pdl`` the chain
+        of GEMM / epilogue / attention kernels uses programmatic dependent
+        launch (each kernel's prologue and weight prefetch overlap the
+        previous kernel's tail)."""
+        ext().set_pdl(self.pdl)
+        try:
+            return self._step()
+        finally:
+            ext().set_pdl(False)
+
+    def _step(self) -> torch.Tensor:
         cfg, st, m = self.cfg, self.store, self.model
         eps = cfg.norm_eps
         x = L.embedding(self.next_in, st.work_of("wte.weight"), out=self.x)
@@ -148,6 +160,13 @@ class DecodeEngine:
         self._graph = None
 
     def sample(self, temperature: float, top_k: int, advance_pos: bool) -> None:
+        ext().set_pdl(self.pdl)
+        try:
+            self._sample(temperature, top_k, advance_pos)
+        finally:
+            ext().set_pdl(False)
+
+    def _sample(self, temperature: float, top_k: int, advance_pos: bool) -> None:
         L.sample_tokens(self.logits, temperature, top_k, self.uniforms, self.gen_count, self.out_tokens, self.next_in,
                         self.pos, advance_pos)
 

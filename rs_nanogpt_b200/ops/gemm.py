@@ -101,7 +101,7 @@ def _skinny_acc(x, w, acc, splits: int):
     if splits <= 0:
         tiles = (n + 127) // 128
         splits = max(1, min((k + 63) // 64, _sms() // tiles))
-    ext().gemm(w, False, x, False, c, ATOMIC_F32_T, 1.0, None, None, splits, 128)
+    ext().gemm_skinny_acc(w, x, c, splits)
     return c
 
 

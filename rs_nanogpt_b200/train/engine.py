@@ -44,7 +44,7 @@ class TrainEngine:
         else:
             from ..models.reference import ReferenceGpt
             self.model = ReferenceGpt(store, torch.float32)
-        if comm == "fused" and self.dist.world_size() > 1:
+        if comm == "fused" and self.dist.world_size() > 1 and store.device.type == "cuda":
             from ..parallel.fused_ddp import FusedDdp
             self.fused_ddp = FusedDdp(store, self.opt, self.dist)
 

@@ -219,3 +219,25 @@ def test_qkv_decode_gemm_matches_separate_kernels():
     _close(k2, k1, 2e-2)
     _close(v2, v1, 2e-2)
     assert acc.abs().sum().item() == 0
+
+
+def test_decode_step_with_programmatic_dependent_launch_is_exact():
+    """The PDL launch chain computes exactly what plain stream order does."""
+    from rs_nanogpt_b200.models.decode import DecodeEngine
+    torch.manual_seed(8)
+    cfg, store = _engine_setup(depth=4)
+    outs = []
+    for pdl in (False, True):
+        eng = DecodeEngine(store, 8, 300)
+        eng.pdl = pdl
+        ids = torch.randint(0, cfg.vocab_size, (8, 256), device="cuda")
+        lens = torch.tensor([256, 1, 100, 37, 200, 5, 64, 128], device="cuda", dtype=torch.int32)
+        torch.manual_seed(9)
+        eng.prefill(ids, lens)
+        res = []
+        for s in range(4):
+            eng.next_in.copy_(torch.arange(8, device="cuda") * (s + 3))
+            res.append(eng.step().clone())
+            eng.pos.add_(1)
+        outs.append(torch.stack(res))
+    assert torch.equal(outs[0], outs[1])
