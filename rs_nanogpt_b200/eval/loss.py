@@ -20,6 +20,8 @@ class EvalMetrics:
 
 
 class BpbAccumulator:
+    """Host accumulator (the reference's per-batch host copy)."""
+
     def __init__(self):
         self.nats_loss = 0.0
         self.valid_tokens = 0
@@ -52,12 +54,37 @@ class BpbAccumulator:
         return self.metrics_from_sums(self.sums())
 
 
+class DeviceBpbAccumulator:
+    """The same four sums kept on the loss's device (float64): one masked
+    reduction per batch and a single host read at the end instead of a
+    device-to-host copy of every batch's per-position losses."""
+
+    def __init__(self, token_bytes: np.ndarray, device):
+        self.device = torch.device(device)
+        self.table = torch.as_tensor(np.asarray(token_bytes, dtype=np.int64), device=self.device)
+        self.acc = torch.zeros(4, dtype=torch.float64, device=self.device)
+
+    def add(self, loss2d: torch.Tensor, targets: torch.Tensor) -> None:
+        loss = loss2d.reshape(-1).to(self.device, torch.float64)
+        tg = targets.reshape(-1).to(self.device)
+        valid = tg >= 0
+        b = torch.where(valid, self.table[tg.clamp(min=0)], torch.zeros_like(tg))
+        has = b > 0
+        self.acc += torch.stack([torch.where(valid, loss, 0.0).sum(), valid.sum().double(),
+                                 torch.where(has, loss, 0.0).sum(), b.sum().double()])
+
+    def sums(self) -> List[float]:
+        return [float(v) for v in self.acc.tolist()]
+
+
 def evaluate_shard_sums(engine, batches, token_bytes: np.ndarray, shard: int = 0, num_shards: int = 1) -> List[float]:
     """Score val batches i with i % num_shards == shard."""
     if not (num_shards >= 1 and 0 <= shard < num_shards):
         raise ValueError(f"invalid shard {shard} / {num_shards}")
-    acc = BpbAccumulator()
+    acc = None
     for batch in list(batches)[shard::num_shards]:
         loss2d = engine.eval_nll(batch.inputs, batch.targets)
-        acc.add(loss2d, batch.targets, token_bytes)
-    return acc.sums()
+        if acc is None:
+            acc = DeviceBpbAccumulator(token_bytes, loss2d.device)
+        acc.add(loss2d, batch.targets)
+    return acc.sums() if acc is not None else [0.0, 0.0, 0.0, 0.0]

@@ -69,19 +69,23 @@ class TrainEngine:
         return s.detach(), cnt
 
     def step(self, batches: Sequence[Tuple[torch.Tensor, torch.Tensor]], tokens_per_step: int, lr_mult: float,
-             targets_may_be_ignored: bool = False) -> StepStats:
+             targets_may_be_ignored: bool = False, on_micro=None) -> StepStats:
+        """One optimizer step over the micro-batches; ``on_micro(i)`` (if
+        given) runs after micro-batch i (per-micro-batch telemetry)."""
         st = self.store
         st.zero_grad()
         inv = 1.0 / tokens_per_step
         nll_sum = torch.zeros((), dtype=torch.float32, device=st.device)
         count = torch.zeros((), dtype=torch.float32, device=st.device)
-        for inputs, targets in batches:
+        for i, (inputs, targets) in enumerate(batches):
             b, t = inputs.shape
             assert len(batches) * b * t == tokens_per_step, (
                 f"batch shape ({b}, {t}) x grad_accum disagrees with tokens_per_step {tokens_per_step}")
             s, c = self.micro_backward(inputs, targets, inv)
             nll_sum += s
             count += c
+            if on_micro is not None:
+                on_micro(i)
         grad_scale = 1.0
         if targets_may_be_ignored:
             # expected * world / global count (== 1 when nothing is ignored).

@@ -110,12 +110,20 @@ def train(engine: TrainEngine, batches, cfg: TrainConfig, ev: EvalContext, fault
     micro-batch (host-side fault injection for tests)."""
     from ..eval.sample import SampleOptions, cached_model, generate_ids
 
+    from ..utils.mem import MemProbe
+
     dist = engine.dist
     store = engine.store
     dist.broadcast_params(store.master)
     store.refresh_work()
     best = math.inf
     t_start = time.perf_counter()
+    probe = MemProbe.from_env(store.device) if dist.is_master() else None
+    if probe is not None:
+        s0 = probe.stats()
+        print(f"mem init         | {s0.summary()}", flush=True)
+        ev.metrics.log(0, "mem", time.perf_counter() - t_start, **s0.record_fields())
+        probe.reset_highs()
     win_t, win_step = time.perf_counter(), 0
     for step in range(cfg.num_iters + 1):
         last = step == cfg.num_iters
@@ -151,8 +159,15 @@ def train(engine: TrainEngine, batches, cfg: TrainConfig, ev: EvalContext, fault
                 fault(step, i)
             b = batches.next_batch()
             micro.append((b.inputs, b.targets))
+        nvtx = store.device.type == "cuda"
+        if nvtx:
+            torch.cuda.nvtx.range_push(f"step {step}")
         mult = lr_mult(step, cfg.num_iters, cfg.warmup_steps, cfg.warmdown_ratio, cfg.final_lr_frac)
-        stats = engine.step(micro, cfg.tokens_per_step, mult, cfg.targets_may_be_ignored)
+        stats = engine.step(micro, cfg.tokens_per_step, mult, cfg.targets_may_be_ignored,
+                            on_micro=(lambda i: print(f"mem step {step:>6} micro {i:>3} | {probe.stats().summary()}",
+                                                      flush=True)) if probe is not None and probe.per_micro() else None)
+        if nvtx:
+            torch.cuda.nvtx.range_pop()
         if logging:
             s, c = dist.all_reduce_sums([float(stats.nll_sum.item()), float(stats.valid_count.item())])
             mean_ce = float(np.float32(s) / np.float32(c)) if c > 0 else math.nan
@@ -180,5 +195,10 @@ def train(engine: TrainEngine, batches, cfg: TrainConfig, ev: EvalContext, fault
                     rate = {}
                 ev.metrics.log(step, "train", elapsed, train_loss=mean_ce, grad_norm=gnorm, lr_matrix=lrs.matrix,
                                lr_embedding=lrs.embedding, lr_unembedding=lrs.unembedding, **rate)
+                if probe is not None:
+                    ms_ = probe.stats()
+                    print(f"mem step {step:>6}   | {ms_.summary()}", flush=True)
+                    ev.metrics.log(step, "mem", elapsed, **ms_.record_fields())
+                    probe.reset_highs()
             win_t, win_step = now, step
     return best

@@ -266,3 +266,26 @@ def test_non_finite_loss_aborts():
     from rs_nanogpt_b200.train.train_loop import TrainingError, check_finite
     with pytest.raises(TrainingError, match="non-finite"):
         check_finite(float("nan"), 3)
+
+
+def test_device_bpb_accumulator_matches_host():
+    from rs_nanogpt_b200.eval.loss import BpbAccumulator, DeviceBpbAccumulator
+    torch.manual_seed(0)
+    tb = np.random.RandomState(0).randint(0, 5, size=50).astype(np.uint32)
+    host, dev = BpbAccumulator(), DeviceBpbAccumulator(tb, "cpu")
+    for _ in range(3):
+        loss = torch.rand(2, 7) * 5
+        tg = torch.randint(-1, 50, (2, 7))
+        host.add(loss, tg, tb)
+        dev.add(loss, tg)
+    assert np.allclose(host.sums(), dev.sums(), rtol=1e-12)
+
+
+def test_mem_trace_env_parsing():
+    from rs_nanogpt_b200.utils.mem import MemProbe, PoolStats, parse_verbosity
+    assert parse_verbosity(None) is None and parse_verbosity("0") is None and parse_verbosity("") is None
+    assert parse_verbosity("1") == 1 and parse_verbosity("2") == 2 and parse_verbosity("3") is None
+    assert MemProbe.from_env("cpu", {"RS_NANOGPT_MEM_TRACE": "1"}) is None  # no pool to read on the CPU
+    s = PoolStats(reserved=10, used=4, reserved_high=12, used_high=6, dev_free=1, dev_total=2)
+    assert s.fragmentation() == 6 and PoolStats(reserved=1, used=5).fragmentation() == 0
+    assert "frag" in s.summary() and s.record_fields()["mem_reserved_high"] == 12
