@@ -72,11 +72,15 @@ constexpr int kEpiWarps = 8, kThreads = 64 + 32 * kEpiWarps;
 template <int BN, bool PAIR>
 struct Smem {
   static constexpr int kBRows = PAIR ? BN / 2 : BN;  // B rows this CTA holds (a pair splits N)
-  static constexpr int kStages = (PAIR || BN == 128) ? 6 : 4;
+  // Pairs move 2/3 of the bytes per FLOP, so they trade a pipeline stage for
+  // four epilogue staging buffers per warp (stores of one chunk overlap the
+  // next chunk; the next residual tile is prefetched).
+  static constexpr int kStages = PAIR ? 5 : (BN == 128 ? 6 : 4);
+  static constexpr int kEpiBufs = PAIR ? 4 : 2;
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = kBRows * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kTotal = kStages * kStageBytes + kEpiWarps * 2 * 2048 /*epilogue staging*/ +
+  static constexpr int kTotal = kStages * kStageBytes + kEpiWarps * kEpiBufs * 2048 /*epilogue staging*/ +
                                 1024 /*align*/ + 512 /*barriers*/;
 };
 
@@ -170,13 +174,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int STAGES = S::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* staging = smem + STAGES * S::kStageBytes;  // kEpiWarps x 2 x 2 KB, 1024-aligned
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(staging + kEpiWarps * 2 * kStageBufBytes);
+  uint8_t* staging = smem + STAGES * S::kStageBytes;  // kEpiWarps x kEpiBufs x 2 KB, 1024-aligned
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(staging + kEpiWarps * S::kEpiBufs * kStageBufBytes);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* acc_full = empty_bar + STAGES;
   uint64_t* acc_empty = acc_full + 2;
-  uint64_t* aux_bar = acc_empty + 2;  // one per epilogue warp
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bar + kEpiWarps);
+  uint64_t* aux_bar = acc_empty + 2;  // two per epilogue warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bar + 2 * kEpiWarps);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int units = args.num_m * args.num_n * args.splits;
@@ -192,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], PAIR ? 2 * kEpiWarps : kEpiWarps);
     }
-    for (int w = 0; w < kEpiWarps; ++w) mbar_init(&aux_bar[w], 1);
+    for (int w = 0; w < 2 * kEpiWarps; ++w) mbar_init(&aux_bar[w], 1);
     fence_barrier_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
@@ -304,11 +308,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ew = warp - 2;                // epilogue warp index
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
     const int half = ew / 4;                // which half of the tile's columns
-    uint8_t* buf_o = staging + ew * 2 * kStageBufBytes;
-    uint8_t* buf_x = buf_o + kStageBufBytes;
+    constexpr int NB = S::kEpiBufs;
+    uint8_t* wbuf = staging + ew * NB * kStageBufBytes;
+    // Chunk ck of this warp stages its output in bufO(ck) and its second
+    // output / residual input in bufX(ck); with four buffers consecutive
+    // chunks alternate between two buffer pairs.
+    auto bufO = [&](int ck) { return wbuf + ((2 * ck) % NB) * kStageBufBytes; };
+    auto bufX = [&](int ck) { return wbuf + ((2 * ck + 1) % NB) * kStageBufBytes; };
     const bool atomic = args.mode == kAtomicF32 || args.mode == kAtomicF32T;
     const bool need_aux = args.mode == kResidual || args.mode == kDRelu2;
-    uint32_t aux_phase = 0;
+    uint32_t aux_ph[2] = {0u, 0u};
+    int ck = 0;
+    auto issue_aux = [&](int ckk, int col, int row) {  // all lanes call; lane 0 issues
+      fence_proxy_async();  // earlier generic reads of the buffer precede the TMA write
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&aux_bar[2 * ew + (ckk & 1)], kStageBufBytes);
+        tma_load_2d(bufX(ckk), &tmX, &aux_bar[2 * ew + (ckk & 1)], col, row);
+      }
+    };
     bool ok = true;
     int local = 0;
     auto release_acc = [&](int b) {
@@ -358,11 +376,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i) x[i] = hv[c4 * 32 + i] / denom;
           if (lane == 0) bulk_wait_read<0>();
           __syncwarp();
-          stage_row_store(buf_o, lane, x);
+          stage_row_store(wbuf, lane, x);
           fence_proxy_async();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmC, buf_o, colb + c4 * 32, row0);
+            tma_store_2d(&tmC, wbuf, colb + c4 * 32, row0);
             bulk_commit();
           }
         }
@@ -371,15 +389,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) release_acc(b);
         continue;
       }
+      const int c_begin = half * (BN / 64), c_end = (half + 1) * (BN / 64);
+      if (need_aux && n * BN + c_begin * 32 < args.N) issue_aux(ck, n * BN + c_begin * 32, row0);
 #pragma unroll 1
-      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+      for (int c = c_begin; c < c_end; ++c) {
         const int col0 = n * BN + c * 32;
         if (col0 >= args.N) break;  // uniform across the warp
-        if (need_aux && lane == 0) {
-          fence_proxy_async();  // earlier reads of buf_x precede the new load
-          mbar_arrive_expect_tx(&aux_bar[ew], kStageBufBytes);
-          tma_load_2d(buf_x, &tmX, &aux_bar[ew], col0, row0);
-        }
+        if (need_aux && NB >= 4 && c + 1 < c_end && col0 + 32 < args.N) issue_aux(ck + 1, col0 + 32, row0);
         float v[32];
         tmem_ld_32x32(tmem_base + (uint32_t(q * 32) << 16) + b * BN + c * 32, v);
         if (atomic) {
@@ -391,10 +407,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) x[i] = args.alpha * v[i];
         if (need_aux) {
-          if (!mbar_wait(&aux_bar[ew], aux_phase, kErrTimeoutEpilogue, args.err)) { ok = false; break; }
-          aux_phase ^= 1;
+          if (!mbar_wait(&aux_bar[2 * ew + (ck & 1)], aux_ph[ck & 1], kErrTimeoutEpilogue, args.err)) {
+            ok = false;
+            break;
+          }
+          aux_ph[ck & 1] ^= 1;
           float y[32];
-          stage_row_load(buf_x, lane, y);
+          stage_row_load(bufX(ck), lane, y);
           if (args.mode == kDRelu2) {
 #pragma unroll
             for (int i = 0; i < 32; ++i)  // d/dh relu(h)^2 = 2 relu(h), on the bf16-rounded upstream grad
@@ -403,11 +422,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) x[i] = __bfloat162float(__float2bfloat16(x[i])) + y[i];
           }
+          // NB == 2: the next chunk's residual load reuses this buffer.
+          if (NB < 4 && c + 1 < c_end && col0 + 32 < args.N) issue_aux(ck + 1, col0 + 32, row0);
         }
-        if (lane == 0) bulk_wait_read<0>();  // the previous chunk's stores have left the buffers
+        // The stores that last read this chunk's buffers (NB / 2 chunks ago) are done.
+        if (lane == 0) bulk_wait_read<NB / 2 - 1>();
         __syncwarp();
         if (args.mode == kRelu2) {
-          stage_row_store(buf_x, lane, x);  // pre-activation h
+          stage_row_store(bufX(ck), lane, x);  // pre-activation h
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             // Square the bf16-rounded pre-activation, as relu(h)^2 on a bf16 h would.
@@ -415,14 +437,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             x[i] = hr * hr;
           }
         }
-        stage_row_store(buf_o, lane, x);
+        stage_row_store(bufO(ck), lane, x);
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmC, buf_o, col0, row0);
-          if (args.mode == kRelu2) tma_store_2d(&tmX, buf_x, col0, row0);
+          tma_store_2d(&tmC, bufO(ck), col0, row0);
+          if (args.mode == kRelu2) tma_store_2d(&tmX, bufX(ck), col0, row0);
           bulk_commit();
         }
+        ++ck;
       }
       tc_fence_before();
       __syncwarp();
@@ -489,14 +512,15 @@ static void launch(const GemmArgs& args, const CUtensorMap& ta, const CUtensorMa
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "gemm launch failed");
 }
 
-// CTA pairs (cta_group::2) for the large 256-column GEMMs; NANOGPT_GEMM_PAIR=0
-// selects single-CTA tiles everywhere.
-static bool pair_enabled() {
-  static const bool on = [] {
+// CTA pairs (cta_group::2) for the large 256-column GEMMs. NANOGPT_GEMM_PAIR:
+// unset/1 = where measured faster (below), 0 = never, 2 = for every eligible
+// product (measurement switch).
+static int pair_mode() {
+  static const int mode = [] {
     const char* e = std::getenv("NANOGPT_GEMM_PAIR");
-    return !(e && e[0] == '0');
+    return e ? std::atoi(e) : 1;
   }();
-  return on;
+  return mode;
 }
 
 static void check_bf16_2d(const torch::Tensor& t, int64_t rows, int64_t cols, const char* what) {
@@ -558,8 +582,12 @@ void gemm_impl(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_majo
   const int BN = block_n == 128 ? 128 : 256;
   // Pairs measured faster than single-CTA tiles only for the weight-gradient
   // products (both operands MN-major); elsewhere single-CTA tiles win.
-  const bool pair = BN == 256 && M > BM && a_mn_major && b_mn_major && mode != kRopeNorm && mode != kAtomicF32T &&
-                    pair_enabled();
+  // Measured at the d20 shapes: pairs win for the weight-gradient products
+  // (both operands MN-major, +6-20%) and the wide lm_head forward (+6%);
+  // single-CTA tiles win or tie elsewhere.
+  const bool pair_default = (a_mn_major && b_mn_major) || (!a_mn_major && !b_mn_major && N >= 32768);
+  const bool pair = BN == 256 && M > BM && mode != kRopeNorm && mode != kAtomicF32T &&
+                    (pair_mode() == 2 || (pair_mode() == 1 && pair_default));
   args.num_m = (M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM);
   args.num_n = (N + BN - 1) / BN;
   args.kb_total = (K + BK - 1) / BK;
