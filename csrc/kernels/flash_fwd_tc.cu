@@ -177,19 +177,22 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
       if (!mbar_wait(&s_full[t], j & 1, kErrTimeoutEpilogue, a.err)) { ok = false; break; }
       tc_fence_after();
       const bool diag = j == nblk - 1;
-      // Pass 1: row max of the scaled scores.
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        float v[32];
-        tmem_ld_32x32(t_s + c * 32, v);
+      // The whole S row in registers (two 64-column loads): row max, then
+      // P = exp2(s * scale*log2e - m) from the same registers. Only the
+      // diagonal block needs the causal mask (keys past the query get -inf).
+      float sv[BN];
+      tmem_ld_32x64(t_s, *reinterpret_cast<float(*)[64]>(sv));
+      tmem_ld_32x64(t_s + 64, *reinterpret_cast<float(*)[64]>(sv + 64));
+      if (diag) {
+        const int lim = qrow - j * BN;  // keys 0..lim of this block are visible
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int key = j * BN + c * 32 + i;
-          const float s = (diag && key > qrow) ? -INFINITY : v[i] * a.sl2;
-          mx = fmaxf(mx, s);
-        }
+        for (int i = 0; i < BN; ++i)
+          if (i > lim) sv[i] = -INFINITY;
       }
+      float mraw = sv[0];
+#pragma unroll
+      for (int i = 1; i < BN; ++i) mraw = fmaxf(mraw, sv[i]);
+      const float mx = mraw * a.sl2;  // sl2 > 0: max commutes with the scale
       // The previous P V must be done before P is rewritten or O rescaled.
       if (j > 0 && !mbar_wait(&o_done[t], (j - 1) & 1, kErrTimeoutEpilogue, a.err)) { ok = false; break; }
       tc_fence_after();
@@ -210,18 +213,15 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
         l *= alpha;
         m_used = m_new;
       }
-      // Pass 2: P = exp2(s - m_used) -> bf16 in shared memory.
+      // P = exp2(s - m_used) -> bf16 in shared memory.
       float rs = 0.f;
-#pragma unroll 1
+#pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
-        float v[32];
-        tmem_ld_32x32(t_s + c * 32, v);
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const int key = j * BN + c * 32 + i;
-          const float p0 = (diag && key > qrow) ? 0.f : exp2f(v[i] * a.sl2 - m_used);
-          const float p1 = (diag && key + 1 > qrow) ? 0.f : exp2f(v[i + 1] * a.sl2 - m_used);
+          const float p0 = exp2f(fmaf(sv[c * 32 + i], a.sl2, -m_used));
+          const float p1 = exp2f(fmaf(sv[c * 32 + i + 1], a.sl2, -m_used));
           rs += p0 + p1;
           pk[i / 2] = pack_bf16x2(p0, p1);
         }
