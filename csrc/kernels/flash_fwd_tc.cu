@@ -36,7 +36,7 @@ constexpr int HD = 128, BM = 128, BN = 128;
 constexpr int kThreads = 320;
 constexpr int kTileBytes = BM * HD * 2;      // 32 KB: Q tile, K block, V block or P tile
 constexpr int kSubBytes = 128 * 64 * 2;      // 16 KB: one 64-column swizzle sub-tile
-constexpr int kSmem = 6 * kTileBytes + 1024 + 256;
+constexpr int kSmem = 7 * kTileBytes + 1024 + 256;
 constexpr float kRescaleThreshold = 8.0f;    // log2 units
 }  // namespace fa
 
@@ -61,19 +61,19 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                       // 2 tiles
-  uint8_t* sK = smem + 2 * kTileBytes;
-  uint8_t* sV = smem + 3 * kTileBytes;
-  uint8_t* sP = smem + 4 * kTileBytes;      // 2 tiles
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTileBytes);
+  uint8_t* sK = smem + 2 * kTileBytes;      // 2 buffers
+  uint8_t* sV = smem + 4 * kTileBytes;
+  uint8_t* sP = smem + 5 * kTileBytes;      // 2 tiles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 7 * kTileBytes);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = bars + 2;
-  uint64_t* v_full = bars + 3;
-  uint64_t* v_empty = bars + 4;
-  uint64_t* s_full = bars + 5;   // [2]
-  uint64_t* p_full = bars + 7;   // [2]
-  uint64_t* o_done = bars + 9;   // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;
+  uint64_t* v_empty = bars + 6;
+  uint64_t* s_full = bars + 7;   // [2]
+  uint64_t* p_full = bars + 9;   // [2]
+  uint64_t* o_done = bars + 11;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int qb = gridDim.x - 1 - blockIdx.x;  // longest rows first
@@ -84,8 +84,10 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    mbar_init(k_full, 1);
-    mbar_init(k_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
     mbar_init(v_full, 1);
     mbar_init(v_empty, 1);
     for (int t = 0; t < 2; ++t) {
@@ -109,56 +111,70 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
         for (int s = 0; s < 2; ++s)
           tma_load_3d(sQ + t * kTileBytes + s * kSubBytes, &tm, q_full, xq + 64 * s, q0 + t * BM, b);
       for (int j = 0; j < nblk1; ++j) {
-        const uint32_t ph = j & 1;
-        if (!mbar_wait(k_empty, ph ^ 1, kErrTimeoutProducer, a.err)) break;
-        mbar_arrive_expect_tx(k_full, kTileBytes);
-        for (int s = 0; s < 2; ++s) tma_load_3d(sK + s * kSubBytes, &tm, k_full, xk + 64 * s, j * BN, b);
-        if (!mbar_wait(v_empty, ph ^ 1, kErrTimeoutProducer, a.err)) break;
+        const int kb = j & 1;
+        if (!mbar_wait(&k_empty[kb], ((j >> 1) & 1) ^ 1, kErrTimeoutProducer, a.err)) break;
+        mbar_arrive_expect_tx(&k_full[kb], kTileBytes);
+        for (int s = 0; s < 2; ++s)
+          tma_load_3d(sK + kb * kTileBytes + s * kSubBytes, &tm, &k_full[kb], xk + 64 * s, j * BN, b);
+        if (!mbar_wait(v_empty, (j & 1) ^ 1, kErrTimeoutProducer, a.err)) break;
         mbar_arrive_expect_tx(v_full, kTileBytes);
         for (int s = 0; s < 2; ++s) tma_load_3d(sV + s * kSubBytes, &tm, v_full, xv + 64 * s, j * BN, b);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
+      // Ping-pong: once tile t's softmax of block j is done, issue O_t += P_t V_j
+      // and then S_t = Q_t K_{j+1}, so each tile's softmax overlaps the other
+      // tile's MMAs. K is double-buffered; V_j is released after PV_1(j).
       const uint32_t id_s = idesc_bf16(BM, BN, false, false);  // Q K^T: both K-major
       const uint32_t id_o = idesc_bf16(BM, HD, false, true);   // P V: V is MN-major (d contiguous)
-      bool ok = mbar_wait(q_full, 0, kErrTimeoutMma, a.err);
+      const int nblk0 = nblk1 - 1;
+      auto issue_s = [&](int t, int j) {
+        const uint32_t q = smem_u32(sQ + t * kTileBytes), k = smem_u32(sK + (j & 1) * kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kSubBytes + (kk & 3) * 32;
+          umma_bf16(tmem + t * BN, sw128_desc(q + off, 16, 1024), sw128_desc(k + off, 16, 1024), id_s,
+                    kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t p = smem_u32(sP + t * kTileBytes), v = smem_u32(sV);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint32_t poff = (kk >> 2) * kSubBytes + (kk & 3) * 32;
+          umma_bf16(tmem + 256 + t * HD, sw128_desc(p + poff, 16, 1024), sw128_desc(v + kk * 2048, kSubBytes, 1024),
+                    id_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&o_done[t]);
+      };
+      bool ok = mbar_wait(q_full, 0, kErrTimeoutMma, a.err) && mbar_wait(&k_full[0], 0, kErrTimeoutMma, a.err);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);  // tile 0 has at least one block
+        issue_s(1, 0);
+        umma_commit(&k_empty[0]);
+      }
       for (int j = 0; j < nblk1 && ok; ++j) {
-        const uint32_t ph = j & 1;
-        if (!mbar_wait(k_full, ph, kErrTimeoutMma, a.err)) break;
-        tc_fence_after();
-        for (int t = 0; t < 2; ++t) {
-          if (j >= nblk1 - 1 + t) continue;  // tile 0 skips the last key block
-          if (j > 0 && !mbar_wait(&p_full[t], (j - 1) & 1, kErrTimeoutMma, a.err)) { ok = false; break; }
+        const bool next = j + 1 < nblk1;  // tile 1 (and tile 0 if j + 1 < nblk0) has block j + 1
+        if (!mbar_wait(v_full, j & 1, kErrTimeoutMma, a.err)) break;
+        if (j < nblk0) {
+          if (!mbar_wait(&p_full[0], j & 1, kErrTimeoutMma, a.err)) break;
           tc_fence_after();
-          const uint32_t q = smem_u32(sQ + t * kTileBytes), k = smem_u32(sK);
-#pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kSubBytes + (kk & 3) * 32;
-            umma_bf16(tmem + t * BN, sw128_desc(q + off, 16, 1024), sw128_desc(k + off, 16, 1024), id_s,
-                      kk > 0 ? 1u : 0u);
-          }
-          umma_commit(&s_full[t]);
+          issue_pv(0, j);
         }
-        if (!ok) break;
-        umma_commit(k_empty);
-        if (!mbar_wait(v_full, ph, kErrTimeoutMma, a.err)) break;
+        if (next && !mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, kErrTimeoutMma, a.err)) break;
         tc_fence_after();
-        for (int t = 0; t < 2; ++t) {
-          if (j >= nblk1 - 1 + t) continue;
-          if (!mbar_wait(&p_full[t], j & 1, kErrTimeoutMma, a.err)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t p = smem_u32(sP + t * kTileBytes), v = smem_u32(sV);
-#pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk) {
-            const uint32_t poff = (kk >> 2) * kSubBytes + (kk & 3) * 32;
-            umma_bf16(tmem + 256 + t * HD, sw128_desc(p + poff, 16, 1024), sw128_desc(v + kk * 2048, kSubBytes, 1024),
-                      id_o, (j > 0 || kk > 0) ? 1u : 0u);
-          }
-          umma_commit(&o_done[t]);
-        }
-        if (!ok) break;
+        if (j + 1 < nblk0) issue_s(0, j + 1);
+        if (!mbar_wait(&p_full[1], j & 1, kErrTimeoutMma, a.err)) break;
+        tc_fence_after();
+        issue_pv(1, j);
         umma_commit(v_empty);
+        if (next) {
+          issue_s(1, j + 1);
+          umma_commit(&k_empty[(j + 1) & 1]);
+        }
       }
     }
   } else {
