@@ -170,13 +170,13 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
           umma_bf16(tmem + 256, sw128_desc(ds + aoff, 16, 1024), sw128_desc(q + kk * 2048, kSub, 1024), id_kn,
                     (n > 0 || kk > 0) ? 1u : 0u);
         }
+        umma_commit(qd_empty);  // Q_j / dO_j are no longer read: the next block's loads may start
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {  // contraction over the 128 keys
           umma_bf16(tmem + 128, sw128_desc(ds + kk * 2048, kSub, 1024), sw128_desc(k + kk * 2048, kSub, 1024),
                     id_nn, kk > 0);
         }
         umma_commit(dq_full);
-        umma_commit(qd_empty);
       }
       umma_commit(kv_done);
     }
@@ -223,8 +223,9 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       const int j = kb + n;
       if (!mbar_wait(st_full, n & 1, kErrTimeoutEpilogue, a.err)) { ok = false; break; }
       tc_fence_after();
-      // P^T / dS^T tiles are free once the previous block's MMAs finished.
-      if (n > 0 && !mbar_wait(qd_empty, (n - 1) & 1, kErrTimeoutEpilogue, a.err)) { ok = false; break; }
+      // P^T / dS^T tiles are free once the previous block's MMAs (the last is
+      // dQ, which reads dS^T) finished.
+      if (n > 0 && !mbar_wait(dq_full, (n - 1) & 1, kErrTimeoutEpilogue, a.err)) { ok = false; break; }
       if (n == 0) {  // the diagonal block: causal mask
         chunk(2 * half, j, true);
         chunk(2 * half + 1, j, true);
