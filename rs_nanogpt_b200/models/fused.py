@@ -159,16 +159,20 @@ class FusedGpt:
         return gemm.linear(hf, self._w("lm_head.weight")).view(b, t, -1)
 
     @torch.no_grad()
-    def forward_backward(self, idx: torch.Tensor, targets: torch.Tensor, loss_scale: float):
+    def forward_backward(self, idx: torch.Tensor, targets: torch.Tensor, loss_scale: float, grad_ready=None):
         """One micro-batch. Gradients of ``loss_scale * sum(nll)`` are added to
-        the store's fp32 gradient buffer. Returns the per-position NLL and
-        the validity mask (device tensors)."""
+        the store's fp32 gradient buffer; ``grad_ready(bucket)`` is called
+        (on the compute stream's timeline) when a bucket's gradient is final:
+        "lm_head" after the loss head, each block index after its weight
+        gradients, "wte" at the end. Returns the per-position NLL."""
         cfg, st = self.cfg, self.store
         b, t = idx.shape
         eps = cfg.norm_eps
         ws = self.workspace(b, t, True)
         hf = self._forward_blocks(idx, ws, train=True)
         nll = self._loss_head(hf, targets, ws, loss_scale)
+        if grad_ready is not None:
+            grad_ready("lm_head")
         # Final norm backward: dx = d rms(x_L).
         dx = L.rmsnorm_bwd(ws.x[cfg.n_layer], ws.dhf, ws.rstdf, dx=ws.dx, accumulate=False)
         for i in reversed(range(cfg.n_layer)):
@@ -189,6 +193,10 @@ class FusedGpt:
                 L.rope_qknorm_bwd(ws.qkv[i], ws.dqkv, ws.rstd_qk[i], self.cos, self.sin, t, cfg.n_head)
             gemm.linear_wgrad(ws.dqkv, ws.h1[i], st.qkv_grad(i))
             gemm.linear_dgrad(ws.dqkv, st.qkv_work(i), out=ws.dh)
+            if grad_ready is not None:
+                grad_ready(i)  # block i's weights are no longer read and its gradient is final
             L.rmsnorm_bwd(ws.x[i], ws.dh, ws.rstd1[i], dx=dx, accumulate=True)
         L.embedding_bwd(idx, dx, st.grad_of("wte.weight"))
+        if grad_ready is not None:
+            grad_ready("wte")
         return nll

@@ -60,14 +60,30 @@ class FusedDdp:
         self.h_pads = symm.rendezvous(pads, name)
         store.grad, store.work = grad, work
         self._keep = (grad, work, pads)
-        shard = (total + self.world - 1) // self.world
-        self.shard = (shard + SHARD_ALIGN - 1) // SHARD_ALIGN * SHARD_ALIGN
-        self.lo = min(total, self.rank * self.shard)
-        self.hi = min(total, self.lo + self.shard)
         self.epoch = 0
         self.sumsq = torch.zeros(1, dtype=torch.float64, device=dev)
         for lo, hi in opt.ranges.values():
             assert lo % 4 == 0 and hi % 4 == 0, "parameter groups must be 4-element aligned"
+        # Buckets in the order the backward completes them: lm_head (its
+        # gradient is final after the loss head), blocks L-1 .. 0, wte.
+        cfg = store.cfg
+        def span(names):
+            lo = min(store.slots[n].offset for n in names)
+            hi = max(store.slots[n].offset + store.slots[n].numel for n in names)
+            return lo, (hi + 3) // 4 * 4
+        self.bucket_ids = ["lm_head"] + [i for i in reversed(range(cfg.n_layer))] + ["wte"]
+        self.buckets = {"lm_head": span(["lm_head.weight"]), "wte": span(["wte.weight"])}
+        for i in range(cfg.n_layer):
+            self.buckets[i] = span([n for n in store.names() if n.startswith(f"blocks.{i}.")])
+        # This rank's shard of every bucket (bucket-local striping, 64-aligned).
+        self.shards = {}
+        for key, (lo, hi) in self.buckets.items():
+            sh = ((hi - lo + self.world - 1) // self.world + SHARD_ALIGN - 1) // SHARD_ALIGN * SHARD_ALIGN
+            s_lo = min(hi, lo + self.rank * sh)
+            self.shards[key] = (s_lo, min(hi, s_lo + sh), sh)
+        self.comm_stream = torch.cuda.Stream(device=dev)
+        self._groups_t = None
+        self._grad_scale = 1.0
 
     def _barrier(self) -> None:
         self.epoch += 1
@@ -84,14 +100,46 @@ class FusedDdp:
                          1.0 / (1.0 - b1 ** t), 1.0 / (1.0 - b2 ** t)])
         return torch.tensor(rows, dtype=torch.float64)
 
-    def reduce_and_step(self, grad_scale: float = 1.0) -> None:
+    def _bucket_kernel(self, key) -> None:
+        lo, hi, _ = self.shards[key]
+        if hi > lo:
+            ext().ddp_rs_adam_ag(int(self.h_grad.buffer_ptrs_dev), int(self.h_work.buffer_ptrs_dev), self.world,
+                                 self.store.master, self.opt.m, self.opt.v, lo, hi, self._groups_t,
+                                 self._grad_scale / self.world, self.sumsq)
+
+    # -- one optimizer step ---------------------------------------------------------
+
+    def begin_step(self, grad_scale: float = 1.0) -> None:
+        """Fix the step's AdamW hyper-parameters (call after set_lr_mult)."""
         self.opt.step_t += 1
-        st = self.store
-        self._barrier()
+        self._groups_t = self._groups()
+        self._grad_scale = grad_scale
         self.sumsq.zero_()
-        ext().ddp_rs_adam_ag(int(self.h_grad.buffer_ptrs_dev), int(self.h_work.buffer_ptrs_dev), self.world,
-                             st.master, self.opt.m, self.opt.v, self.lo, self.hi, self._groups(),
-                             grad_scale / self.world, self.sumsq)
+
+    def bucket_ready(self, key) -> None:
+        """Called on the compute stream once this rank's gradient of bucket
+        `key` is final: the bucket's barrier + reduce-scatter/AdamW/all-gather
+        run on the communication stream while the backward continues."""
+        ev = torch.cuda.Event()
+        ev.record()
+        self.comm_stream.wait_event(ev)
+        with torch.cuda.stream(self.comm_stream):
+            self._barrier()        # every rank's gradient of this bucket is final
+            self._bucket_kernel(key)
+
+    def finish_step(self) -> None:
+        """Closing barrier (all peers finished reading this rank's gradients and
+        writing its weights); the compute stream waits for it."""
+        with torch.cuda.stream(self.comm_stream):
+            self._barrier()
+        torch.cuda.current_stream().wait_stream(self.comm_stream)
+
+    def reduce_and_step(self, grad_scale: float = 1.0) -> None:
+        """The whole step after the backward (no overlap)."""
+        self.begin_step(grad_scale)
+        self._barrier()
+        for key in self.bucket_ids:
+            self._bucket_kernel(key)
         self._barrier()
 
     def grad_norm(self) -> float:
@@ -102,9 +150,11 @@ class FusedDdp:
         """Make every rank's fp32 master complete again (after sharded updates)."""
         import torch.distributed as td
         st = self.store
-        pad = self.shard * self.world
-        full = torch.zeros(pad, dtype=torch.float32, device=st.device)
-        full[: st.total].copy_(st.master)
-        mine = full[self.rank * self.shard:(self.rank + 1) * self.shard].clone()
-        td.all_gather_into_tensor(full, mine)
-        st.master.copy_(full[: st.total])
+        for key in self.bucket_ids:
+            lo, hi = self.buckets[key]
+            s_lo, s_hi, sh = self.shards[key]
+            full = torch.zeros(sh * self.world, dtype=torch.float32, device=st.device)
+            mine = torch.zeros(sh, dtype=torch.float32, device=st.device)
+            mine[: s_hi - s_lo].copy_(st.master[s_lo:s_hi])
+            td.all_gather_into_tensor(full, mine)
+            st.master[lo:hi].copy_(full[: hi - lo])

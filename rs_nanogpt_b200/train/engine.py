@@ -49,11 +49,13 @@ class TrainEngine:
             self.fused_ddp = FusedDdp(store, self.opt, self.dist)
 
     # -- pieces ---------------------------------------------------------------------
-    def micro_backward(self, inputs: torch.Tensor, targets: torch.Tensor, loss_scale: float) -> Tuple[torch.Tensor, torch.Tensor]:
+    def micro_backward(self, inputs: torch.Tensor, targets: torch.Tensor, loss_scale: float,
+                       grad_ready=None) -> Tuple[torch.Tensor, torch.Tensor]:
         """Adds d(loss_scale * sum nll)/dtheta to the gradient buffer; returns
-        (sum nll, valid count) as device scalars."""
+        (sum nll, valid count) as device scalars. ``grad_ready(bucket)`` (CUDA
+        path) is called as each bucket's gradient becomes final."""
         if self.store.device.type == "cuda":
-            nll = self.model.forward_backward(inputs, targets, loss_scale)
+            nll = self.model.forward_backward(inputs, targets, loss_scale, grad_ready=grad_ready)
             valid = (targets.reshape(-1) >= 0).sum(dtype=torch.float32)
             return nll.sum(), valid
         from ..models.reference import cross_entropy_sum_count
@@ -77,15 +79,29 @@ class TrainEngine:
         inv = 1.0 / tokens_per_step
         nll_sum = torch.zeros((), dtype=torch.float32, device=st.device)
         count = torch.zeros((), dtype=torch.float32, device=st.device)
+        # With the fused data-parallel kernel and a loss scale known in advance
+        # (pretraining), the last micro-batch's backward hands each finished
+        # gradient bucket to the communication stream: reduce-scatter, AdamW
+        # and all-gather of layer i overlap the backward of layers < i.
+        overlap = self.fused_ddp is not None and not targets_may_be_ignored
+        if overlap:
+            self.opt.set_lr_mult(lr_mult)
         for i, (inputs, targets) in enumerate(batches):
             b, t = inputs.shape
             assert len(batches) * b * t == tokens_per_step, (
                 f"batch shape ({b}, {t}) x grad_accum disagrees with tokens_per_step {tokens_per_step}")
-            s, c = self.micro_backward(inputs, targets, inv)
+            last = i == len(batches) - 1
+            if overlap and last:
+                self.fused_ddp.begin_step(1.0)
+            s, c = self.micro_backward(inputs, targets, inv,
+                                       grad_ready=self.fused_ddp.bucket_ready if overlap and last else None)
             nll_sum += s
             count += c
             if on_micro is not None:
                 on_micro(i)
+        if overlap:
+            self.fused_ddp.finish_step()
+            return StepStats(nll_sum, count)
         grad_scale = 1.0
         if targets_may_be_ignored:
             # expected * world / global count (== 1 when nothing is ignored).

@@ -25,8 +25,7 @@ torch.cuda.set_device(env.local_rank)
 dev = torch.device("cuda", env.local_rank)
 dist = DistCtx.init(env, "nccl", dev)
 cfg = GptConfig(vocab_size=1024, sequence_len=128, n_layer=2, n_head=2, n_embd=256, rope_base=10000.0)
-engines = {}
-for backend in ("nccl", "fused"):
+def make(backend):
     st = ParamStore(cfg, dev)
     init_params(st, seed=5, mode="bench")
     g = torch.Generator(device=dev).manual_seed(9)
@@ -34,33 +33,39 @@ for backend in ("nccl", "fused"):
         if n.endswith("c_proj.weight"):
             st.param(n).normal_(0, 0.02, generator=g)
     st.refresh_work()
-    engines[backend] = TrainEngine(st, GroupLrs(0.2, 0.004, 0.003), dist=dist, comm=backend)
+    return TrainEngine(st, GroupLrs(0.2, 0.004, 0.003), dist=dist, comm=backend)
 g = torch.Generator(device=dev).manual_seed(100 + dist.rank())
 batches = []
 for _ in range(3):
     x = torch.randint(0, 1024, (2, 129), device=dev, generator=g)
     batches.append((x[:, :-1].contiguous(), x[:, 1:].contiguous()))
-# Identical non-trivial optimizer state, then ONE step each: the split-K
-# weight gradients use fp32 atomics, so multi-step runs are not bitwise
-# reproducible and Adam would amplify that noise on near-zero gradients.
-norms = {}
-for backend, eng in engines.items():
-    gm = torch.Generator(device=dev).manual_seed(77)
-    eng.opt.m.copy_(torch.randn(eng.opt.m.shape, device=dev, generator=gm) * 1e-3)
-    eng.opt.v.copy_(torch.rand(eng.opt.v.shape, device=dev, generator=gm) * 1e-5)
-    eng.opt.step_t = 4
-    eng.step(batches[:2], 512, 0.7)
-    norms[backend] = eng.grad_norm()
-    eng.sync_master()
-torch.cuda.synchronize()
-a, b = engines["nccl"].store, engines["fused"].store
-diff = (a.master - b.master).abs().max().item()
-wdiff = (a.work.float() - b.work.float()).abs().max().item()
-print(f"rank {dist.rank()} master diff {diff:.3e} work diff {wdiff:.3e} norms {norms}", flush=True)
-assert kernel_status() == 0
-assert diff < 1e-5, diff
-assert wdiff < 1e-2, wdiff
-assert abs(norms["nccl"] - norms["fused"]) < 1e-3 * max(1.0, norms["nccl"])
+# ignored=False: the fused step overlaps the last micro-batch's backward
+# (per-bucket reduce-scatter/AdamW/all-gather on a side stream);
+# ignored=True: the SFT path (global valid-count scale) runs after the backward.
+for ignored in (False, True):
+    engines = {backend: make(backend) for backend in ("nccl", "fused")}
+    # Identical non-trivial optimizer state, then ONE step each: the split-K
+    # weight gradients use fp32 atomics, so multi-step runs are not bitwise
+    # reproducible and Adam would amplify that noise on near-zero gradients.
+    norms = {}
+    for backend, eng in engines.items():
+        gm = torch.Generator(device=dev).manual_seed(77)
+        eng.opt.m.copy_(torch.randn(eng.opt.m.shape, device=dev, generator=gm) * 1e-3)
+        eng.opt.v.copy_(torch.rand(eng.opt.v.shape, device=dev, generator=gm) * 1e-5)
+        eng.opt.step_t = 4
+        eng.step(batches[:2], 512, 0.7, targets_may_be_ignored=ignored)
+        norms[backend] = eng.grad_norm()
+        eng.sync_master()
+    torch.cuda.synchronize()
+    a, b = engines["nccl"].store, engines["fused"].store
+    diff = (a.master - b.master).abs().max().item()
+    wdiff = (a.work.float() - b.work.float()).abs().max().item()
+    print(f"rank {dist.rank()} ignored={ignored} master diff {diff:.3e} work diff {wdiff:.3e} norms {norms}",
+          flush=True)
+    assert kernel_status() == 0
+    assert diff < 1e-5, diff
+    assert wdiff < 1e-2, wdiff
+    assert abs(norms["nccl"] - norms["fused"]) < 1e-3 * max(1.0, norms["nccl"])
 dist.shutdown()
 os._exit(0)
 """
