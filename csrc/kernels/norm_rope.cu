@@ -86,16 +86,29 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x, const __
   if (row >= rows) return;
   const long off = long(row) * C;
   const float r = rstd[row];
-  float xv[VPT][8], gv[VPT][8];
+  // All three inputs of the row (x, dy and, when accumulating, dx) are
+  // loaded up front as packed bf16 so their latencies overlap.
+  uint4 xw[VPT], gw[VPT], dw[VPT];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    if (c < C) {
+      xw[i] = *reinterpret_cast<const uint4*>(x + off + c);
+      gw[i] = *reinterpret_cast<const uint4*>(dy + off + c);
+      if (accum) dw[i] = *reinterpret_cast<const uint4*>(dx + off + c);
+    }
+  }
   float dot = 0.f;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int c = (i * 32 + lane) * 8;
     if (c < C) {
-      load8(x + off + c, xv[i]);
-      load8(dy + off + c, gv[i]);
+      const uint32_t xs[4] = {xw[i].x, xw[i].y, xw[i].z, xw[i].w}, gs[4] = {gw[i].x, gw[i].y, gw[i].z, gw[i].w};
 #pragma unroll
-      for (int j = 0; j < 8; ++j) dot += gv[i][j] * xv[i][j];
+      for (int j = 0; j < 4; ++j) {
+        const float2 xf = unpack_bf16x2(xs[j]), gf = unpack_bf16x2(gs[j]);
+        dot += gf.x * xf.x + gf.y * xf.y;
+      }
     }
   }
   dot = warp_sum(dot) * r * r / C;  // r^2 * mean(dy * x)
@@ -103,14 +116,21 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x, const __
   for (int i = 0; i < VPT; ++i) {
     const int c = (i * 32 + lane) * 8;
     if (c < C) {
-      float o[8];
-      if (accum) load8(dx + off + c, o);
+      const uint32_t xs[4] = {xw[i].x, xw[i].y, xw[i].z, xw[i].w}, gs[4] = {gw[i].x, gw[i].y, gw[i].z, gw[i].w};
+      const uint32_t ds[4] = {dw[i].x, dw[i].y, dw[i].z, dw[i].w};
+      uint32_t o[4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float g = r * (gv[i][j] - xv[i][j] * dot);
-        o[j] = accum ? o[j] + g : g;
+      for (int j = 0; j < 4; ++j) {
+        const float2 xf = unpack_bf16x2(xs[j]), gf = unpack_bf16x2(gs[j]);
+        float g0 = r * (gf.x - xf.x * dot), g1 = r * (gf.y - xf.y * dot);
+        if (accum) {
+          const float2 df = unpack_bf16x2(ds[j]);
+          g0 += df.x;
+          g1 += df.y;
+        }
+        o[j] = pack_bf16x2(g0, g1);
       }
-      store8(dx + off + c, o);
+      *reinterpret_cast<uint4*>(dx + off + c) = make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
 }
