@@ -200,6 +200,17 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster_addr) {
                : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16: the A tile (M = 128 lanes x
+// K = 16) sits in 8 TMEM columns, two bf16 per 32-bit column (lower K index in
+// the low half).
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
 // Arrive on `bar` once all previously issued tcgen05.mma of this thread complete.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -238,6 +249,17 @@ __device__ __forceinline__ void tmem_ld_32x64(uint32_t taddr, float (&v)[64]) {
       : "memory");
 #pragma unroll
   for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Each thread writes 16 32-bit columns of its lane; waits for completion.
+__device__ __forceinline__ void tmem_st_32x16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
 }
 
 // Inverse of tmem_ld_32x32: each thread writes its lane's 32 columns.

@@ -13,7 +13,9 @@
 //   MMA5  dQ_j = dS K                -> TMEM [128,256) (dS^T's smem tile read as
 //                                       an MN-major A operand: no transpose copy)
 //   (drain warpgroup, thread = query row) dQ_j * scale is added to an fp32
-//   accumulator with vector atomics.
+//   accumulator with TMA reduce-add tensor stores, staged through dS^T's
+//   shared-memory tile once MMA5 has consumed it.
+// Q_j / dO_j (and their LSE / D rows) are double-buffered.
 // After the last block the compute warpgroup writes dK * scale and dV (bf16)
 // into the gradient buffer. A final small kernel converts the dQ accumulator
 // to bf16.
@@ -38,7 +40,10 @@ constexpr int kThreads = 448;  // 2 + 8 compute + 4 drain warps
 constexpr int kTile = 128 * 128 * 2;   // 32 KB
 constexpr int kSub = 128 * 64 * 2;     // 16 KB swizzle sub-tile
 constexpr int kStage = 32 * 32 * 4;  // 4 KB: one drain warp's 32 x 32 fp32 dQ chunk
-constexpr int kSmem = 6 * kTile + 4 * 2 * kStage + 2 * BQ * 4 + 1024 + 256;
+// K, V, Q x2, dO x2, dS^T (also the dQ drain staging) + LSE/D x2 + barriers.
+// No alignment slack: the dynamic shared memory base is checked to be
+// 1024-byte aligned at run time (the kernel reports an error otherwise).
+constexpr int kSmem = 7 * kTile + 2 * 2 * BQ * 4 + 256;
 }  // namespace fb
 
 struct FbArgs {
@@ -68,26 +73,29 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
                         const __grid_constant__ CUtensorMap tmq, const FbArgs a) {
   using namespace fb;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = smem_raw;
+  if (smem_u32(smem) & 1023) {  // uniform: the whole CTA leaves before any barrier or TMEM use
+    if (threadIdx.x == 0) atomicCAS(a.err, 0, kErrTimeoutOther);
+    return;
+  }
   uint8_t* sK = smem;
   uint8_t* sV = smem + kTile;
-  uint8_t* sQ = smem + 2 * kTile;
-  uint8_t* sO = smem + 3 * kTile;   // dO_j
-  uint8_t* sP = smem + 4 * kTile;   // P^T  [key][query]
-  uint8_t* sS = smem + 5 * kTile;   // dS^T [key][query]
-  uint8_t* sStage = smem + 6 * kTile;  // drain warps: 2 x 4 KB each (dQ chunks for TMA reduce-add)
-  float* sL = reinterpret_cast<float*>(smem + 6 * kTile + 8 * kStage);  // lse2 of the query block
-  float* sD = sL + BQ;                                     // D of the query block
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTile + 8 * kStage + 2 * BQ * 4);
+  uint8_t* sQ = smem + 2 * kTile;   // [2] query blocks
+  uint8_t* sO = smem + 4 * kTile;   // [2] dO blocks
+  uint8_t* sS = smem + 6 * kTile;   // dS^T [key][query]; after the dQ product, the drain staging
+  float* sL = reinterpret_cast<float*>(smem + 7 * kTile);  // [2] lse2 of the query block
+  float* sD = sL + 2 * BQ;                                 // [2] D of the query block
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 7 * kTile + 4 * BQ * 4);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qd_full = bars + 1;
-  uint64_t* qd_empty = bars + 2;
-  uint64_t* st_full = bars + 3;
-  uint64_t* p_full = bars + 4;
-  uint64_t* dq_full = bars + 5;
-  uint64_t* dq_free = bars + 6;
-  uint64_t* kv_done = bars + 7;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  uint64_t* qd_full = bars + 1;   // [2]
+  uint64_t* qd_empty = bars + 3;  // [2]
+  uint64_t* st_full = bars + 5;
+  uint64_t* p_full = bars + 6;
+  uint64_t* dq_full = bars + 7;
+  uint64_t* dq_free = bars + 8;
+  uint64_t* kv_done = bars + 9;
+  uint64_t* stage_free = bars + 10;  // the drain's staging reads of dS^T's tile are done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int kb = blockIdx.x;  // key block; low blocks have the most query blocks
@@ -98,13 +106,16 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    mbar_init(qd_full, 1);
-    mbar_init(qd_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qd_full[i], 1);
+      mbar_init(&qd_empty[i], 1);
+    }
     mbar_init(st_full, 1);
     mbar_init(p_full, 8);
     mbar_init(dq_full, 1);
     mbar_init(dq_free, 4);
     mbar_init(kv_done, 1);
+    mbar_init(stage_free, 4);
     fence_barrier_init();
     prefetch_tmap(&tm);
     prefetch_tmap(&tmo);
@@ -124,15 +135,15 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
         tma_load_3d(sV + s * kSub, &tm, kv_full, xv + 64 * s, kb * BK, b);
       }
       for (int n = 0; n < nblk; ++n) {
-        const int j = kb + n;
-        if (n > 0 && !mbar_wait(qd_empty, (n - 1) & 1, kErrTimeoutProducer, a.err)) break;
-        mbar_arrive_expect_tx(qd_full, 2 * kTile + 2 * BQ * 4);
+        const int j = kb + n, u = n & 1;
+        if (!mbar_wait(&qd_empty[u], ((n >> 1) & 1) ^ 1, kErrTimeoutProducer, a.err)) break;
+        mbar_arrive_expect_tx(&qd_full[u], 2 * kTile + 2 * BQ * 4);
         for (int s = 0; s < 2; ++s) {
-          tma_load_3d(sQ + s * kSub, &tm, qd_full, xq + 64 * s, j * BQ, b);
-          tma_load_3d(sO + s * kSub, &tmo, qd_full, h * HD + 64 * s, j * BQ, b);
+          tma_load_3d(sQ + u * kTile + s * kSub, &tm, &qd_full[u], xq + 64 * s, j * BQ, b);
+          tma_load_3d(sO + u * kTile + s * kSub, &tmo, &qd_full[u], h * HD + 64 * s, j * BQ, b);
         }
-        bulk_load(sL, a.lse + bh * a.T + j * BQ, BQ * 4, qd_full);
-        bulk_load(sD, a.dsum + bh * a.T + j * BQ, BQ * 4, qd_full);
+        bulk_load(sL + u * BQ, a.lse + bh * a.T + j * BQ, BQ * 4, &qd_full[u]);
+        bulk_load(sD + u * BQ, a.dsum + bh * a.T + j * BQ, BQ * 4, &qd_full[u]);
       }
     }
   } else if (warp == 1) {
@@ -140,18 +151,20 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       const uint32_t id_kk = idesc_bf16(128, 128, false, false);  // MMA1, MMA2
       const uint32_t id_kn = idesc_bf16(128, HD, false, true);    // MMA3, MMA4: B MN-major
       const uint32_t id_nn = idesc_bf16(128, HD, true, true);     // MMA5: A and B MN-major
-      const uint32_t k = smem_u32(sK), v = smem_u32(sV), q = smem_u32(sQ), o = smem_u32(sO);
-      const uint32_t p = smem_u32(sP), ds = smem_u32(sS);
+      const uint32_t k = smem_u32(sK), v = smem_u32(sV), ds = smem_u32(sS);
       bool ok = mbar_wait(kv_full, 0, kErrTimeoutMma, a.err);
       for (int n = 0; n < nblk && ok; ++n) {
-        if (!mbar_wait(qd_full, n & 1, kErrTimeoutMma, a.err)) break;
+        const int u = n & 1;
+        const uint32_t q = smem_u32(sQ + u * kTile), o = smem_u32(sO + u * kTile);
+        if (!mbar_wait(&qd_full[u], (n >> 1) & 1, kErrTimeoutMma, a.err)) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * kSub + (kk & 3) * 32;
           umma_bf16(tmem + 0, sw128_desc(k + off, 16, 1024), sw128_desc(q + off, 16, 1024), id_kk, kk > 0);
         }
-        // dP^T reuses the columns of the previous dQ: wait until it was drained.
+        // dP^T reuses the columns of the previous dQ (and the compute warps
+        // reuse dS^T's tile, the drain's staging): wait until it was drained.
         if (n > 0 && !mbar_wait(dq_free, (n - 1) & 1, kErrTimeoutMma, a.err)) break;
         tc_fence_after();
 #pragma unroll
@@ -164,13 +177,15 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk) {  // contraction over the 128 queries
+          // P^T is in tensor memory: 32 query columns of chunk c packed as bf16
+          // pairs in TMEM columns [32c, 32c + 16) (written over S^T).
+          umma_bf16_ts(tmem + 384, tmem + 32 * (kk >> 1) + 8 * (kk & 1), sw128_desc(o + kk * 2048, kSub, 1024),
+                       id_kn, (n > 0 || kk > 0) ? 1u : 0u);
           const uint32_t aoff = (kk >> 2) * kSub + (kk & 3) * 32;
-          umma_bf16(tmem + 384, sw128_desc(p + aoff, 16, 1024), sw128_desc(o + kk * 2048, kSub, 1024), id_kn,
-                    (n > 0 || kk > 0) ? 1u : 0u);
           umma_bf16(tmem + 256, sw128_desc(ds + aoff, 16, 1024), sw128_desc(q + kk * 2048, kSub, 1024), id_kn,
                     (n > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(qd_empty);  // Q_j / dO_j are no longer read: the next block's loads may start
+        umma_commit(&qd_empty[u]);  // Q_j / dO_j are no longer read
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {  // contraction over the 128 keys
           umma_bf16(tmem + 128, sw128_desc(ds + kk * 2048, kSub, 1024), sw128_desc(k + kk * 2048, kSub, 1024),
@@ -189,16 +204,19 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
     const int key = kb * BK + r;
     const uint32_t lanes = uint32_t(quarter * 32) << 16;
     bool ok = true;
-    // P^T and dS^T for 32 query columns starting at c * 32.
-    auto chunk = [&](int c, int j, bool diag) {
+    // P^T (into tensor memory, over this chunk's own S^T columns) and dS^T
+    // (shared memory) for the 32 query columns starting at c * 32.
+    auto chunk = [&](int c, int j, bool diag, int u) {
       float s[32], dp[32];
       tmem_ld_32x32(tmem + lanes + c * 32, s);
       tmem_ld_32x32(tmem + lanes + 128 + c * 32, dp);
+      const float* L = sL + u * BQ;
+      const float* D = sD + u * BQ;
       uint32_t pp[16], dd[16];
 #pragma unroll
       for (int i = 0; i < 32; i += 4) {
-        const float4 l4 = *reinterpret_cast<const float4*>(sL + c * 32 + i);
-        const float4 d4 = *reinterpret_cast<const float4*>(sD + c * 32 + i);
+        const float4 l4 = *reinterpret_cast<const float4*>(L + c * 32 + i);
+        const float4 d4 = *reinterpret_cast<const float4*>(D + c * 32 + i);
         const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
         float pv[4], gv[4];
 #pragma unroll
@@ -213,25 +231,25 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
         dd[i / 2] = pack_bf16x2(gv[0], gv[1]);
         dd[i / 2 + 1] = pack_bf16x2(gv[2], gv[3]);
       }
+      tmem_st_32x16(tmem + lanes + c * 32, pp);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        *reinterpret_cast<uint4*>(sP + tile_off(r, c * 4 + u)) = make_uint4(pp[4 * u], pp[4 * u + 1], pp[4 * u + 2], pp[4 * u + 3]);
-        *reinterpret_cast<uint4*>(sS + tile_off(r, c * 4 + u)) = make_uint4(dd[4 * u], dd[4 * u + 1], dd[4 * u + 2], dd[4 * u + 3]);
-      }
+      for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<uint4*>(sS + tile_off(r, c * 4 + q)) = make_uint4(dd[4 * q], dd[4 * q + 1], dd[4 * q + 2], dd[4 * q + 3]);
     };
     for (int n = 0; n < nblk && ok; ++n) {
-      const int j = kb + n;
+      const int j = kb + n, u = n & 1;
       if (!mbar_wait(st_full, n & 1, kErrTimeoutEpilogue, a.err)) { ok = false; break; }
       tc_fence_after();
-      // P^T / dS^T tiles are free once the previous block's MMAs (the last is
-      // dQ, which reads dS^T) finished.
-      if (n > 0 && !mbar_wait(dq_full, (n - 1) & 1, kErrTimeoutEpilogue, a.err)) { ok = false; break; }
+      // st_full of block n comes after the previous block's dQ product and
+      // TMEM drain (dP^T waited for it); dS^T's tile is also the drain's
+      // staging, so wait for its reads too.
+      if (n > 0 && !mbar_wait(stage_free, (n - 1) & 1, kErrTimeoutEpilogue, a.err)) { ok = false; break; }
       if (n == 0) {  // the diagonal block: causal mask
-        chunk(2 * half, j, true);
-        chunk(2 * half + 1, j, true);
+        chunk(2 * half, j, true, u);
+        chunk(2 * half + 1, j, true, u);
       } else {
-        chunk(2 * half, j, false);
-        chunk(2 * half + 1, j, false);
+        chunk(2 * half, j, false, u);
+        chunk(2 * half + 1, j, false, u);
       }
       fence_proxy_async();
       tc_fence_before();
@@ -319,7 +337,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
     // buffers per warp let the next chunk fill while the previous one drains.
     const int quarter = warp & 3;
     const uint32_t lanes = uint32_t(quarter * 32) << 16;
-    uint8_t* stage = sStage + (warp - 10) * 2 * kStage;
+    uint8_t* stage = sS + (warp - 10) * 2 * kStage;  // dS^T's tile: free once dQ = dS K is done
     int chunks = 0;
     for (int n = 0; n < nblk; ++n) {
       const int j = kb + n;
@@ -331,7 +349,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
         tmem_ld_32x32(tmem + lanes + 128 + c * 32, x);
         if (a.dbg & 1) continue;
         uint8_t* buf = stage + (chunks & 1) * kStage;
-        if (lane == 0 && chunks >= 2) bulk_wait_read<1>();  // this buffer's previous reduce has read it
+        if (lane == 0 && c >= 2) bulk_wait_read<1>();  // this buffer's previous reduce has read it
         __syncwarp();
 #pragma unroll
         for (int k = 0; k < 8; ++k)
@@ -348,7 +366,12 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(dq_free);
+      if (lane == 0) mbar_arrive(dq_free);  // dQ's TMEM columns are free for the next dP^T
+      // The staging reads must be done before the compute warps rewrite dS^T.
+      if (lane == 0) {
+        bulk_wait_read<0>();
+        mbar_arrive(stage_free);
+      }
     }
     if (lane == 0) bulk_wait<0>();
   }
