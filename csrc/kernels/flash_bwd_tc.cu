@@ -5,23 +5,26 @@
 // shared memory; for every query block j >= the key block (causal) it
 //   MMA1  S^T  = K  Q_j^T            -> TMEM [0,128)
 //   MMA2  dP^T = V  dO_j^T           -> TMEM [128,256)
-//   (compute warpgroup, thread = key row)
+//   (compute warps, thread = key row)
 //         P^T  = exp2(S^T * scale*log2e - lse2[q])   (causal mask on the diagonal)
-//         dS^T = P^T o (dP^T - D[q])                 both bf16 -> shared memory
-//   MMA3  dV  += P^T  dO_j           -> TMEM [384,512)
+//         dS^T = P^T o (dP^T - D[q])
+//         P^T goes back to tensor memory (bf16 pairs, over the S^T columns just
+//         read); dS^T goes to shared memory.
+//   MMA3  dV  += P^T  dO_j           -> TMEM [384,512) (A operand from TMEM)
 //   MMA4  dK  += dS^T Q_j            -> TMEM [256,384)
 //   MMA5  dQ_j = dS K                -> TMEM [128,256) (dS^T's smem tile read as
 //                                       an MN-major A operand: no transpose copy)
-//   (drain warpgroup, thread = query row) dQ_j * scale is added to an fp32
+//   (drain warps, thread = query row) dQ_j * scale is added to an fp32
 //   accumulator with TMA reduce-add tensor stores, staged through dS^T's
 //   shared-memory tile once MMA5 has consumed it.
 // Q_j / dO_j (and their LSE / D rows) are double-buffered.
-// After the last block the compute warpgroup writes dK * scale and dV (bf16)
-// into the gradient buffer. A final small kernel converts the dQ accumulator
-// to bf16.
+// After the last block the compute warps write dK * scale (with the RoPE /
+// QK-norm backward when requested) and dV (bf16) into the gradient buffer. A
+// final small kernel converts the dQ accumulator to bf16.
 //
-// Warps: 0 = TMA/bulk loads, 1 = TMEM allocation + MMA issue, 2-5 = compute,
-// 6-9 = dQ drain. Every wait is bounded (common.cuh).
+// Warps: 0 = TMA/bulk loads, 1 = TMEM allocation + MMA issue, 2-9 = compute
+// (two per TMEM lane quarter), 10-13 = dQ drain. Every wait is bounded
+// (common.cuh).
 #include <cstdlib>
 
 #include <ATen/cuda/CUDAContext.h>
