@@ -64,6 +64,8 @@ struct FbArgs {
   const float* rope_rstd;
   const float* rope_cos;
   const float* rope_sin;
+  // Measurement switch (NANOGPT_FB_DEBUG; gives wrong gradients when set):
+  // bit 0 skips the dQ reduce-add, bit 1 replaces the softmax-gradient math by copies.
   int dbg;
 };
 
