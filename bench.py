@@ -40,6 +40,7 @@ def parse():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--depth", type=int, default=20)
+    p.add_argument("--vocab", type=int, default=65536, help="vocabulary size (BASELINE config 3, d12: 32768)")
     p.add_argument("--device-batch", type=int, default=32)
     p.add_argument("--seq", type=int, default=2048)
     p.add_argument("--total-batch", type=int, default=TOTAL_BATCH)
@@ -85,7 +86,7 @@ def main():
     device = torch.device("cuda", local)
     dist = DistCtx.init(env, "nccl", device) if env else DistCtx.single(device)
 
-    cfg = d_model(args.depth, vocab_size=65536, sequence_len=args.seq)
+    cfg = d_model(args.depth, vocab_size=args.vocab, sequence_len=args.seq)
     per = n * args.device_batch * args.seq
     if args.total_batch % per:
         raise SystemExit(f"total batch {args.total_batch} is not a multiple of gpus*device_batch*seq {per}")
@@ -161,7 +162,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic uniform-random token ids; random-init weights (N(0,0.02), zero-init projections)",
-            "config": {"model": f"GPT d{args.depth} (n_embd {cfg.n_embd}, {cfg.n_head} heads x 128, vocab 65536)",
+            "config": {"model": f"GPT d{args.depth} (n_embd {cfg.n_embd}, {cfg.n_head} heads x 128, vocab {cfg.vocab_size})",
                        "global_batch": args.total_batch, "seq_len": args.seq, "device_batch": args.device_batch,
                        "grad_accum": accum, "parallelism": f"dp{n}", "comm_backend": args.backend,
                        "l2": "inputs larger than L2 (GB-scale activations per micro-batch)"},

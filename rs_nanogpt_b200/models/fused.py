@@ -81,6 +81,9 @@ class FusedGpt:
         self.cfg = store.cfg
         if self.cfg.head_dim != 128:
             raise ValueError(f"the fused CUDA path supports head_dim 128, got {self.cfg.head_dim}")
+        if self.cfg.vocab_size % 8:
+            raise ValueError(f"the fused CUDA path needs a vocabulary size that is a multiple of 8 (16-byte logits "
+                             f"rows), got {self.cfg.vocab_size}; train the tokenizer with such a --vocab-size")
         cos, sin = rope_tables(self.cfg, store.device)
         self.cos, self.sin = cos.contiguous(), sin.contiguous()
         self._ws: Dict[Tuple[int, int, bool], _Workspace] = {}
