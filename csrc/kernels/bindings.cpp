@@ -32,7 +32,9 @@ bool flash_fwd_tc_supported(int64_t T, int64_t HD);
 void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch::Tensor lse, torch::Tensor dsum,
                   torch::Tensor dq_acc, torch::Tensor dqkv, int64_t B, int64_t T, int64_t H,
                   c10::optional<torch::Tensor> rope_rstd, c10::optional<torch::Tensor> rope_cos,
-                  c10::optional<torch::Tensor> rope_sin);
+                  c10::optional<torch::Tensor> rope_sin, bool prepared);
+void flash_bwd_prep(torch::Tensor out, torch::Tensor dout, torch::Tensor dsum, torch::Tensor dq_acc, int64_t B,
+                    int64_t T, int64_t H);
 bool flash_bwd_tc_supported(int64_t T, int64_t HD);
 void gemm_qkv_rope(torch::Tensor x, torch::Tensor w, torch::Tensor qkv, torch::Tensor rstd, torch::Tensor cos_t,
                    torch::Tensor sin_t, int64_t T, int64_t H, double eps);
@@ -71,7 +73,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_fwd", &nk::flash_fwd);
   m.def("flash_bwd", &nk::flash_bwd);
   m.def("flash_fwd_tc", &nk::flash_fwd_tc);
-  m.def("flash_bwd_tc", &nk::flash_bwd_tc);
+  m.def("flash_bwd_tc", &nk::flash_bwd_tc, py::arg("qkv"), py::arg("out"), py::arg("dout"), py::arg("lse"),
+        py::arg("dsum"), py::arg("dq_acc"), py::arg("dqkv"), py::arg("B"), py::arg("T"), py::arg("H"),
+        py::arg("rope_rstd") = py::none(), py::arg("rope_cos") = py::none(), py::arg("rope_sin") = py::none(),
+        py::arg("prepared") = false);
+  m.def("flash_bwd_prep", &nk::flash_bwd_prep);
   m.def("flash_bwd_tc_supported", &nk::flash_bwd_tc_supported);
   m.def("flash_fwd_tc_supported", &nk::flash_fwd_tc_supported);
   m.def("ddp_barrier", &nk::ddp_barrier);

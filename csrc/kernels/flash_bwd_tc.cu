@@ -446,12 +446,27 @@ static CUtensorMap seq_map_3d(void* base, int64_t B, int64_t T, int64_t width) {
 
 void flash_dsum(torch::Tensor out, torch::Tensor dout, torch::Tensor dsum, int64_t B, int64_t T, int64_t H);
 
-// Full backward with the tcgen05 kernel: D precompute, zeroed fp32 dQ
-// accumulator (caller's scratch), the main kernel, then dQ -> bf16.
+// The backward's memory-bound preparation: D = rowsum(dO o O) and the zeroed
+// fp32 dQ accumulator. Separate so a caller can run it on another stream
+// (next to an independent GEMM) and then call flash_bwd_tc with prepared=true.
+void flash_bwd_prep(torch::Tensor out, torch::Tensor dout, torch::Tensor dsum, torch::Tensor dq_acc, int64_t B,
+                    int64_t T, int64_t H) {
+  TORCH_CHECK(dq_acc.scalar_type() == at::kFloat && dq_acc.is_contiguous() && dq_acc.numel() == B * T * out.size(1),
+              "flash_bwd_prep: dq_acc");
+  const at::cuda::CUDAGuard guard(out.device());
+  flash_dsum(out, dout, dsum, B, T, H);
+  TORCH_CHECK(cudaMemsetAsync(dq_acc.data_ptr(), 0, size_t(dq_acc.numel()) * 4, at::cuda::getCurrentCUDAStream()) ==
+                  cudaSuccess,
+              "flash_bwd_prep: memset");
+}
+
+// Full backward with the tcgen05 kernel: D precompute and zeroed fp32 dQ
+// accumulator (caller's scratch; skipped when `prepared`), the main kernel,
+// then dQ -> bf16.
 void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch::Tensor lse, torch::Tensor dsum,
                   torch::Tensor dq_acc, torch::Tensor dqkv, int64_t B, int64_t T, int64_t H,
                   c10::optional<torch::Tensor> rope_rstd, c10::optional<torch::Tensor> rope_cos,
-                  c10::optional<torch::Tensor> rope_sin) {
+                  c10::optional<torch::Tensor> rope_sin, bool prepared) {
   using namespace fb;
   const int64_t C = qkv.size(1) / 3;
   TORCH_CHECK(qkv.is_contiguous() && dqkv.is_contiguous() && dout.is_contiguous() && out.is_contiguous(),
@@ -465,9 +480,11 @@ void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torc
                   reinterpret_cast<uintptr_t>(dsum.data_ptr()) % 16 == 0, "flash_bwd_tc: 16-byte aligned lse/dsum");
   const at::cuda::CUDAGuard guard(qkv.device());
   auto stream = at::cuda::getCurrentCUDAStream();
-  flash_dsum(out, dout, dsum, B, T, H);
-  TORCH_CHECK(cudaMemsetAsync(dq_acc.data_ptr(), 0, size_t(B * T * C) * 4, stream) == cudaSuccess,
-              "flash_bwd_tc: memset");
+  if (!prepared) {
+    flash_dsum(out, dout, dsum, B, T, H);
+    TORCH_CHECK(cudaMemsetAsync(dq_acc.data_ptr(), 0, size_t(B * T * C) * 4, stream) == cudaSuccess,
+                "flash_bwd_tc: memset");
+  }
   CUtensorMap tm = seq_map_3d(qkv.data_ptr(), B, T, 3 * C);
   CUtensorMap tmo = seq_map_3d(dout.data_ptr(), B, T, C);
   CUtensorMap tmq;

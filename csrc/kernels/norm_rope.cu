@@ -174,7 +174,10 @@ void rmsnorm_bwd(torch::Tensor x, torch::Tensor dy, torch::Tensor rstd, torch::T
   TORCH_CHECK(C % 8 == 0 && C <= 2048 && rstd.numel() == rows, "rmsnorm_bwd: shape");
   const at::cuda::CUDAGuard guard(x.device());
   auto stream = at::cuda::getCurrentCUDAStream();
-  const int warps = 8, grid = (rows + warps - 1) / warps;
+  // Two warps per block: small blocks fit in the registers a running GEMM
+  // leaves free, so the training backward can run this next to a
+  // weight-gradient GEMM on another stream.
+  const int warps = 2, grid = (rows + warps - 1) / warps;
   auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
   auto gp = reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr());
   auto dp = reinterpret_cast<__nv_bfloat16*>(dx.data_ptr());

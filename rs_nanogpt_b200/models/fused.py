@@ -34,6 +34,7 @@ import torch
 from ..config import GptConfig
 from ..ops import gemm
 from ..ops import layers as L
+from ..ops._ext import ext
 from .params import ParamStore
 from .reference import rope_tables
 
@@ -90,6 +91,11 @@ class FusedGpt:
         # RoPE + QK-norm live in the QKV GEMM epilogue (forward) and in the
         # attention backward's dQ/dK write-out when the shapes allow it.
         self.fuse_rope = gemm.qkv_rope_supported(self.cfg.n_embd, self.cfg.head_dim)
+
+    def _side_stream(self) -> torch.cuda.Stream:
+        if getattr(self, "_side", None) is None:
+            self._side = torch.cuda.Stream(device=self.store.device)
+        return self._side
 
     def workspace(self, batch: int, seq: int, train: bool) -> _Workspace:
         key = (batch, seq, train)
@@ -178,27 +184,46 @@ class FusedGpt:
             grad_ready("lm_head")
         # Final norm backward: dx = d rms(x_L).
         dx = L.rmsnorm_bwd(ws.x[cfg.n_layer], ws.dhf, ws.rstdf, dx=ws.dx, accumulate=False)
+        # The memory-bound steps (the two RMSNorm backwards, the attention
+        # backward's D = rowsum(dO o O) and dQ-accumulator clearing) run on a
+        # side stream next to an independent weight-gradient GEMM; the main
+        # stream waits for them before anything that reads their output.
+        main = torch.cuda.current_stream()
+        side = self._side_stream()
+
+        def on_side(fn):
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                fn()
+
         for i in reversed(range(cfg.n_layer)):
             p = f"blocks.{i}."
             w_mlp, w_fc = self._w(p + "mlp.c_proj.weight"), self._w(p + "mlp.c_fc.weight")
             # MLP: x'' = x' + relu(h2 Wfc^T)^2 Wmlp^T
             gemm.linear_wgrad(dx, ws.act[i], st.grad_of(p + "mlp.c_proj.weight"))
             gemm.linear_dgrad_drelu2(dx, w_mlp, ws.hpre[i], out=ws.dact)
-            gemm.linear_wgrad(ws.dact, ws.h2[i], st.grad_of(p + "mlp.c_fc.weight"))
             gemm.linear_dgrad(ws.dact, w_fc, out=ws.dh)
-            L.rmsnorm_bwd(ws.xmid[i], ws.dh, ws.rstd2[i], dx=dx, accumulate=True)
+            on_side(lambda: L.rmsnorm_bwd(ws.xmid[i], ws.dh, ws.rstd2[i], dx=dx, accumulate=True))
+            gemm.linear_wgrad(ws.dact, ws.h2[i], st.grad_of(p + "mlp.c_fc.weight"))
+            main.wait_stream(side)
             # Attention: x' = x + attn(rms(x)) Wproj^T
-            gemm.linear_wgrad(dx, ws.y[i], st.grad_of(p + "attn.c_proj.weight"))
             gemm.linear_dgrad(dx, self._w(p + "attn.c_proj.weight"), out=ws.dy)
+            use_tc = ext().flash_bwd_tc_supported(t, cfg.head_dim)
+            if use_tc:
+                on_side(lambda: L.flash_bwd_prep(ws.y[i], ws.dy, ws.dsum, ws.dq_acc, b, t, cfg.n_head))
+            gemm.linear_wgrad(dx, ws.y[i], st.grad_of(p + "attn.c_proj.weight"))
+            main.wait_stream(side)
             folded = L.flash_attention_bwd(ws.qkv[i], ws.y[i], ws.dy, ws.lse[i], ws.dsum, ws.dqkv, b, t, cfg.n_head,
-                                           dq_acc=ws.dq_acc, rope=(ws.rstd_qk[i], self.cos, self.sin))
+                                           dq_acc=ws.dq_acc, rope=(ws.rstd_qk[i], self.cos, self.sin),
+                                           prepared=use_tc)
             if not folded:
                 L.rope_qknorm_bwd(ws.qkv[i], ws.dqkv, ws.rstd_qk[i], self.cos, self.sin, t, cfg.n_head)
-            gemm.linear_wgrad(ws.dqkv, ws.h1[i], st.qkv_grad(i))
             gemm.linear_dgrad(ws.dqkv, st.qkv_work(i), out=ws.dh)
+            on_side(lambda: L.rmsnorm_bwd(ws.x[i], ws.dh, ws.rstd1[i], dx=dx, accumulate=True))
+            gemm.linear_wgrad(ws.dqkv, ws.h1[i], st.qkv_grad(i))
+            main.wait_stream(side)
             if grad_ready is not None:
                 grad_ready(i)  # block i's weights are no longer read and its gradient is final
-            L.rmsnorm_bwd(ws.x[i], ws.dh, ws.rstd1[i], dx=dx, accumulate=True)
         L.embedding_bwd(idx, dx, st.grad_of("wte.weight"))
         if grad_ready is not None:
             grad_ready("wte")

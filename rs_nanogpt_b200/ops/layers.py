@@ -70,20 +70,28 @@ def flash_attention(qkv, out, lse, batch: int, seq_len: int, n_head: int, impl: 
         ext().flash_fwd(qkv, out, lse, batch, seq_len, n_head)
 
 
+def flash_bwd_prep(out, dout, dsum, dq_acc, batch: int, seq_len: int, n_head: int) -> None:
+    """D = rowsum(dO o O) and a zeroed dQ accumulator for the tcgen05 backward
+    (memory-bound; may run on another stream before ``flash_attention_bwd(...,
+    prepared=True)``)."""
+    ext().flash_bwd_prep(out, dout, dsum, dq_acc, batch, seq_len, n_head)
+
+
 def flash_attention_bwd(qkv, out, dout, lse, dsum, dqkv, batch: int, seq_len: int, n_head: int,
-                        dq_acc=None, impl: str = "auto", rope=None) -> bool:
+                        dq_acc=None, impl: str = "auto", rope=None, prepared: bool = False) -> bool:
     """Causal attention backward into dqkv (dQ | dK | dV). The tcgen05 kernel
     (head_dim 128, seq_len % 128 == 0) needs ``dq_acc``, an fp32 (tokens, C)
     scratch buffer for the dQ accumulation; without it the mma.sync kernels run.
     ``rope=(rstd, cos, sin)`` folds the RoPE + QK-norm backward into the dQ/dK
-    write-out (tcgen05 path only). Returns True when that fold happened."""
+    write-out (tcgen05 path only). ``prepared``: ``flash_bwd_prep`` already ran
+    (tcgen05 path). Returns True when that fold happened."""
     hd = qkv.shape[1] // 3 // n_head
     use_tc = impl == "tc" or (impl == "auto" and dq_acc is not None and ext().flash_bwd_tc_supported(seq_len, hd))
     if use_tc:
         r = rope if rope is not None else (None, None, None)
-        ext().flash_bwd_tc(qkv, out, dout, lse, dsum, dq_acc, dqkv, batch, seq_len, n_head, *r)
+        ext().flash_bwd_tc(qkv, out, dout, lse, dsum, dq_acc, dqkv, batch, seq_len, n_head, *r, prepared)
         return rope is not None
-    ext().flash_bwd(qkv, out, dout, lse, dsum, dqkv, batch, seq_len, n_head)
+    ext().flash_bwd(qkv, out, dout, lse, dsum, dqkv, batch, seq_len, n_head)  # computes its own D
     return False
 
 
