@@ -32,12 +32,13 @@ namespace nk {
 
 enum GemmMode : int {
   kStoreBf16 = 0,   // C = alpha*acc
-  kRelu2 = 1,       // C = relu(alpha*acc)^2, AUX_OUT = alpha*acc
+  kRelu2 = 1,       // C = relu(alpha*acc)^2, AUX_OUT = alpha*acc (AUX_OUT optional)
   kDRelu2 = 2,      // C = alpha*acc * 2*relu(AUX)
   kResidual = 3,    // C = alpha*acc + AUX (AUX may alias C)
   kAtomicF32 = 4,   // C(fp32) += alpha*acc   (split-K capable)
   kRopeNorm = 5,    // QKV projection: q and k heads get RoPE + RMSNorm over head_dim, v stored plain
   kAtomicF32T = 6,  // C^T(fp32) += alpha*acc: C is [N, M]; a warp's 32 rows hit 32 adjacent floats
+  kDRelu2Act = 7,   // C = alpha*acc * 2*sqrt(AUX), AUX = relu(h)^2 (the ReLU^2 output)
 };
 
 struct GemmArgs {
@@ -108,6 +109,15 @@ __device__ __forceinline__ void unit_coords(const GemmArgs& a, int u, int& m, in
 constexpr int kStageBufBytes = 2048;
 
 __device__ __forceinline__ uint32_t stg_off(int r, int j) { return uint32_t(r * 64 + ((j ^ ((r >> 1) & 3)) << 4)); }
+
+// Hardware square root (sqrt.approx, ~1 ulp): far below the bf16 rounding of
+// the value it scales, and a single instruction where the IEEE-rounded sqrtf
+// path costs the epilogue half its throughput.
+__device__ __forceinline__ float sqrt_approx(float x) {
+  float r;
+  asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
 
 __device__ __forceinline__ void stage_row_store(uint8_t* buf, int r, const float (&x)[32]) {
 #pragma unroll
@@ -316,7 +326,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto bufO = [&](int ck) { return wbuf + ((2 * ck) % NB) * kStageBufBytes; };
     auto bufX = [&](int ck) { return wbuf + ((2 * ck + 1) % NB) * kStageBufBytes; };
     const bool atomic = args.mode == kAtomicF32 || args.mode == kAtomicF32T;
-    const bool need_aux = args.mode == kResidual || args.mode == kDRelu2;
+    const bool need_aux = args.mode == kResidual || args.mode == kDRelu2 || args.mode == kDRelu2Act;
+    const bool keep_h = args.mode == kRelu2 && args.aux_out != nullptr;
     uint32_t aux_ph[2] = {0u, 0u};
     int ck = 0;
     auto issue_aux = [&](int ckk, int col, int row) {  // all lanes call; lane 0 issues
@@ -418,6 +429,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i)  // d/dh relu(h)^2 = 2 relu(h), on the bf16-rounded upstream grad
               x[i] = __bfloat162float(__float2bfloat16(x[i])) * 2.f * fmaxf(y[i], 0.f);
+          } else if (args.mode == kDRelu2Act) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)  // relu(h) = sqrt(relu(h)^2): the pre-activation need not be kept
+              x[i] = __bfloat162float(__float2bfloat16(x[i])) * 2.f * sqrt_approx(fmaxf(y[i], 0.f));
           } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i) x[i] = __bfloat162float(__float2bfloat16(x[i])) + y[i];
@@ -429,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) bulk_wait_read<NB / 2 - 1>();
         __syncwarp();
         if (args.mode == kRelu2) {
-          stage_row_store(bufX(ck), lane, x);  // pre-activation h
+          if (keep_h) stage_row_store(bufX(ck), lane, x);  // pre-activation h
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             // Square the bf16-rounded pre-activation, as relu(h)^2 on a bf16 h would.
@@ -442,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) {
           tma_store_2d(&tmC, bufO(ck), col0, row0);
-          if (args.mode == kRelu2) tma_store_2d(&tmX, bufX(ck), col0, row0);
+          if (keep_h) tma_store_2d(&tmX, bufX(ck), col0, row0);
           bulk_commit();
         }
         ++ck;
@@ -567,14 +582,13 @@ void gemm_impl(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_majo
     args.rope_cos = rope->rope_cos; args.rope_sin = rope->rope_sin; args.rope_rstd = rope->rope_rstd;
     args.rope_T = rope->rope_T; args.rope_H = rope->rope_H; args.rope_C = rope->rope_C; args.rope_eps = rope->rope_eps;
   }
-  if (mode == kDRelu2 || mode == kResidual) {
+  if (mode == kDRelu2 || mode == kDRelu2Act || mode == kResidual) {
     TORCH_CHECK(aux.has_value(), "gemm: mode needs aux");
     check_bf16_2d(*aux, M, N, "aux");
     args.aux = reinterpret_cast<const __nv_bfloat16*>(aux->data_ptr());
     args.ld_aux = aux->stride(0);
   }
-  if (mode == kRelu2) {
-    TORCH_CHECK(aux_out.has_value(), "gemm: relu2 needs aux_out");
+  if (mode == kRelu2 && aux_out.has_value()) {
     check_bf16_2d(*aux_out, M, N, "aux_out");
     args.aux_out = reinterpret_cast<__nv_bfloat16*>(aux_out->data_ptr());
     args.ld_aux_out = aux_out->stride(0);
@@ -605,9 +619,9 @@ void gemm_impl(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_majo
   CUtensorMap tc = ta, tx = ta;
   if (!f32out) {
     tc = make_tmap_bf16_2d_swz(C.data_ptr(), N, M, C.stride(0), 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
-    if (mode == kResidual || mode == kDRelu2)
+    if (mode == kResidual || mode == kDRelu2 || mode == kDRelu2Act)
       tx = make_tmap_bf16_2d_swz(aux->data_ptr(), N, M, aux->stride(0), 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
-    else if (mode == kRelu2)
+    else if (mode == kRelu2 && aux_out.has_value())
       tx = make_tmap_bf16_2d_swz(aux_out->data_ptr(), N, M, aux_out->stride(0), 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
   }
   const at::cuda::CUDAGuard guard(A.device());
@@ -621,6 +635,7 @@ void gemm(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_major, to
           double alpha, c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> aux_out, int64_t splits,
           int64_t block_n) {
   TORCH_CHECK(mode != kRopeNorm, "gemm: use gemm_qkv_rope for the RoPE epilogue");
+  TORCH_CHECK(mode >= kStoreBf16 && mode <= kDRelu2Act, "gemm: unknown epilogue mode");
   gemm_impl(A, a_mn_major, B, b_mn_major, C, mode, alpha, aux, aux_out, splits, block_n, nullptr);
 }
 

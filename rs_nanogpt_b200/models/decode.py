@@ -63,7 +63,6 @@ class DecodeEngine:
         self.y = torch.empty(batch, c, **bf)
         self.xmid = torch.empty(batch, c, **bf)
         self.act = torch.empty(batch, 4 * c, **bf)
-        self.hpre = torch.empty(batch, 4 * c, **bf)
         self.logits = torch.empty(batch, v, **bf)
         splits = (capacity + chunk - 1) // chunk
         self.part_o = torch.empty(batch * h * splits * 128, **f32)
@@ -144,7 +143,7 @@ class DecodeEngine:
             else:
                 gemm.linear_residual(self.y, w_proj, x, out=self.xmid)
                 L.rmsnorm(self.xmid, eps, out=self.h)
-                gemm.linear_relu2(self.h, w_fc, act=self.act, h=self.hpre)
+                gemm.linear_relu2_act(self.h, w_fc, act=self.act)
                 gemm.linear_residual(self.act, w_mlp, self.xmid, out=x)
                 L.rmsnorm(x, eps, out=self.h)
         gemm.linear(self.h, st.work_of("lm_head.weight"), out=self.logits)  # h = final norm of x

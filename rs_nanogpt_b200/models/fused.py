@@ -27,6 +27,7 @@ residual-stream gradient in place.
 Activation buffers are allocated once per batch shape and reused by every
 micro-batch.
 """
+import os
 from typing import Dict, Optional, Tuple
 
 import torch
@@ -38,7 +39,10 @@ from ..ops._ext import ext
 from .params import ParamStore
 from .reference import rope_tables
 
-XENT_CHUNK_BYTES = 1 << 30  # logits bytes per loss-head chunk
+# Logits bytes per loss-head chunk (NANOGPT_XENT_CHUNK_MB overrides). Larger
+# chunks give the lm_head GEMMs more output tiles per launch (fewer partial
+# waves over the 148 SMs) at the cost of a larger logits buffer.
+XENT_CHUNK_BYTES = int(os.environ.get("NANOGPT_XENT_CHUNK_MB", "1024")) << 20
 
 
 class _Workspace:
@@ -58,7 +62,6 @@ class _Workspace:
         self.h2 = [torch.empty(m, c, **bf) for _ in range(n_keep)]
         self.rstd2 = [torch.empty(m, **f32) for _ in range(n_keep)]
         self.act = [torch.empty(m, 4 * c, **bf) for _ in range(n_keep)]
-        self.hpre = [torch.empty(m, 4 * c, **bf) for _ in range(n_keep)]
         self.hf = torch.empty(m, c, **bf)
         self.rstdf = torch.empty(m, **f32)
         self.nll = torch.empty(m, **f32)
@@ -128,7 +131,7 @@ class FusedGpt:
             L.flash_attention(qkv, ws.y[j], ws.lse[j], b, t, cfg.n_head)
             xmid = gemm.linear_residual(ws.y[j], self._w(p + "attn.c_proj.weight"), x, out=ws.xmid[j])
             h2 = L.rmsnorm(xmid, eps, out=ws.h2[j], rstd=ws.rstd2[j])
-            gemm.linear_relu2(h2, self._w(p + "mlp.c_fc.weight"), act=ws.act[j], h=ws.hpre[j])
+            gemm.linear_relu2_act(h2, self._w(p + "mlp.c_fc.weight"), act=ws.act[j])
             x_next = ws.x[i + 1] if train else ws.x[(i + 1) % 2]
             x = gemm.linear_residual(ws.act[j], self._w(p + "mlp.c_proj.weight"), xmid, out=x_next)
         return L.rmsnorm(x, eps, out=ws.hf, rstd=ws.rstdf)
@@ -201,7 +204,7 @@ class FusedGpt:
             w_mlp, w_fc = self._w(p + "mlp.c_proj.weight"), self._w(p + "mlp.c_fc.weight")
             # MLP: x'' = x' + relu(h2 Wfc^T)^2 Wmlp^T
             gemm.linear_wgrad(dx, ws.act[i], st.grad_of(p + "mlp.c_proj.weight"))
-            gemm.linear_dgrad_drelu2(dx, w_mlp, ws.hpre[i], out=ws.dact)
+            gemm.linear_dgrad_drelu2_act(dx, w_mlp, ws.act[i], out=ws.dact)
             gemm.linear_dgrad(ws.dact, w_fc, out=ws.dh)
             on_side(lambda: L.rmsnorm_bwd(ws.xmid[i], ws.dh, ws.rstd2[i], dx=dx, accumulate=True))
             gemm.linear_wgrad(ws.dact, ws.h2[i], st.grad_of(p + "mlp.c_fc.weight"))

@@ -46,6 +46,16 @@ def linear_relu2(x, w, act=None, h=None):
     return act, h
 
 
+def linear_relu2_act(x, w, act=None):
+    """act = relu(x w^T)^2 (bf16) without keeping the pre-activation; its
+    backward is ``linear_dgrad_drelu2_act``, which recovers relu(h) as
+    sqrt(act)."""
+    if act is None:
+        act = torch.empty(x.shape[0], w.shape[0], device=x.device, dtype=torch.bfloat16)
+    ext().gemm(x, False, w, False, act, RELU2, 1.0, None, None, 1, _block_n(w.shape[0]))
+    return act
+
+
 def linear_residual(x, w, residual, out=None):
     """out = residual + x w^T (out may be `residual` itself)."""
     if out is None:
@@ -82,7 +92,17 @@ def linear_dgrad_drelu2(dy, w, h, out=None):
     return out
 
 
+def linear_dgrad_drelu2_act(dy, w, act, out=None):
+    """dh = (dy @ w) * 2 sqrt(act), act = relu(h)^2: the ReLU^2 backward from
+    the activation alone (2 relu(h) = 2 sqrt(relu(h)^2))."""
+    if out is None:
+        out = torch.empty(dy.shape[0], w.shape[1], device=dy.device, dtype=torch.bfloat16)
+    ext().gemm(dy, False, w, True, out, DRELU2_ACT, 1.0, act, None, 1, _block_n(w.shape[1]))
+    return out
+
+
 ATOMIC_F32_T = 6
+DRELU2_ACT = 7
 
 
 def skinny_ok(m: int) -> bool:

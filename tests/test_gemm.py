@@ -57,6 +57,19 @@ def test_relu2_and_drelu2():
     _close(dh, (dy.float() @ w2.float()) * 2 * torch.relu(h.float()))
 
 
+def test_relu2_act_only_and_backward_from_act():
+    """The training path keeps only act = relu(h)^2 and recovers relu(h) as sqrt(act)."""
+    from rs_nanogpt_b200.ops import gemm
+    torch.manual_seed(3)
+    x, w = _rand(512, 256), _rand(1024, 256, scale=0.1)
+    act = gemm.linear_relu2_act(x, w)
+    h = x.float() @ w.float().t()
+    _close(act, torch.relu(h) ** 2)
+    dy, w2 = _rand(512, 256), _rand(256, 1024)
+    dh = gemm.linear_dgrad_drelu2_act(dy, w2, act)
+    _close(dh, (dy.float() @ w2.float()) * 2 * torch.relu(h))
+
+
 def test_residual_in_place():
     from rs_nanogpt_b200.ops import gemm
     torch.manual_seed(4)
