@@ -61,10 +61,12 @@ struct GemmArgs {
   const float* rope_sin;
   float* rope_rstd;
   int rope_T, rope_H, rope_C;
+  long rope_ld;  // row stride of the transposed (64, >= T) cos/sin tables
   float rope_eps;
   // A (K-major) depends on no earlier kernel (a weight): under programmatic
   // dependent launch its first tiles are fetched before griddepcontrol.wait.
   int a_independent;
+  int rotate;  // single-output epilogues rotate through all staging buffers
 };
 
 constexpr int BM = 128, BK = 64, kGroupM = 16;
@@ -328,6 +330,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool atomic = args.mode == kAtomicF32 || args.mode == kAtomicF32T;
     const bool need_aux = args.mode == kResidual || args.mode == kDRelu2 || args.mode == kDRelu2Act;
     const bool keep_h = args.mode == kRelu2 && args.aux_out != nullptr;
+    // One output and no staged input: every buffer of the warp can hold an
+    // output chunk, so NB - 1 stores may still be reading while the next is written.
+    const bool single_out = args.rotate && !need_aux && !keep_h;
+    auto bufS = [&](int ck) { return single_out ? wbuf + (ck % NB) * kStageBufBytes : bufO(ck); };
     uint32_t aux_ph[2] = {0u, 0u};
     int ck = 0;
     auto issue_aux = [&](int ckk, int col, int row) {  // all lanes call; lane 0 issues
@@ -366,12 +372,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) hv[c4 * 32 + i] = __bfloat162float(__float2bfloat16(args.alpha * v[i]));
         }
-        const float* cr = args.rope_cos + long(pos) * 64;
-        const float* sr = args.rope_sin + long(pos) * 64;
+        // Transposed tables: lane l reads position row0 + l, so each load of
+        // the warp covers consecutive addresses.
+        const float* cr = args.rope_cos + pos;
+        const float* sr = args.rope_sin + pos;
         float ss = 0.f;
 #pragma unroll
         for (int i = 0; i < 64; ++i) {
-          const float cs = __ldg(cr + i), sn = __ldg(sr + i);
+          const float cs = __ldg(cr + i * args.rope_ld), sn = __ldg(sr + i * args.rope_ld);
           const float x1 = hv[i], x2 = hv[i + 64];
           hv[i] = x1 * cs + x2 * sn;       // y1 = x1 cos + x2 sin
           hv[i + 64] = x2 * cs - x1 * sn;  // y2 = x2 cos - x1 sin
@@ -384,16 +392,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c4 = 0; c4 < 4; ++c4) {
           float x[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) x[i] = hv[c4 * 32 + i] / denom;
-          if (lane == 0) bulk_wait_read<0>();
+          for (int i = 0; i < 32; ++i) x[i] = hv[c4 * 32 + i] * inv;
+          uint8_t* sb = bufS(ck);  // same rotation as the plain chunks of this launch
+          if (lane == 0) {
+            if (single_out) bulk_wait_read<NB - 1>();
+            else bulk_wait_read<0>();
+          }
           __syncwarp();
-          stage_row_store(wbuf, lane, x);
+          stage_row_store(sb, lane, x);
           fence_proxy_async();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmC, wbuf, colb + c4 * 32, row0);
+            tma_store_2d(&tmC, sb, colb + c4 * 32, row0);
             bulk_commit();
           }
+          ++ck;
         }
         tc_fence_before();
         __syncwarp();
@@ -441,7 +454,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (NB < 4 && c + 1 < c_end && col0 + 32 < args.N) issue_aux(ck + 1, col0 + 32, row0);
         }
         // The stores that last read this chunk's buffers (NB / 2 chunks ago) are done.
-        if (lane == 0) bulk_wait_read<NB / 2 - 1>();
+        if (lane == 0) {
+          if (single_out) bulk_wait_read<NB - 1>();
+          else bulk_wait_read<NB / 2 - 1>();
+        }
         __syncwarp();
         if (args.mode == kRelu2) {
           if (keep_h) stage_row_store(bufX(ck), lane, x);  // pre-activation h
@@ -452,11 +468,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             x[i] = hr * hr;
           }
         }
-        stage_row_store(bufO(ck), lane, x);
+        stage_row_store(bufS(ck), lane, x);
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmC, bufO(ck), col0, row0);
+          tma_store_2d(&tmC, bufS(ck), col0, row0);
           if (keep_h) tma_store_2d(&tmX, bufX(ck), col0, row0);
           bulk_commit();
         }
@@ -538,6 +554,15 @@ static int pair_mode() {
   return mode;
 }
 
+// NANOGPT_GEMM_ROTATE=0 keeps one staging buffer per output chunk (A/B switch).
+static int rotate_mode() {
+  static const int mode = [] {
+    const char* e = std::getenv("NANOGPT_GEMM_ROTATE");
+    return e ? std::atoi(e) : 1;
+  }();
+  return mode;
+}
+
 static void check_bf16_2d(const torch::Tensor& t, int64_t rows, int64_t cols, const char* what) {
   TORCH_CHECK(t.scalar_type() == at::kBFloat16 && t.dim() == 2 && t.size(0) == rows && t.size(1) == cols &&
                   t.stride(1) == 1 && (t.stride(0) * 2) % 16 == 0 &&
@@ -578,9 +603,10 @@ void gemm_impl(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_majo
   args.ldc = C.stride(0);
   args.err = error_word();
   args.a_independent = a_independent ? 1 : 0;
+  args.rotate = rotate_mode();
   if (rope) {
     args.rope_cos = rope->rope_cos; args.rope_sin = rope->rope_sin; args.rope_rstd = rope->rope_rstd;
-    args.rope_T = rope->rope_T; args.rope_H = rope->rope_H; args.rope_C = rope->rope_C; args.rope_eps = rope->rope_eps;
+    args.rope_T = rope->rope_T; args.rope_ld = rope->rope_ld; args.rope_H = rope->rope_H; args.rope_C = rope->rope_C; args.rope_eps = rope->rope_eps;
   }
   if (mode == kDRelu2 || mode == kDRelu2Act || mode == kResidual) {
     TORCH_CHECK(aux.has_value(), "gemm: mode needs aux");
@@ -641,18 +667,20 @@ void gemm(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_major, to
 
 // qkv[M, 3C] = x[M, C] . w[3C, C]^T with RoPE + QK-RMSNorm fused into the
 // epilogue for the q and k column blocks (head_dim 128, 3C % 256 == 0).
+// cos_t / sin_t are the RoPE tables transposed: (64, >= T), position fastest.
 void gemm_qkv_rope(torch::Tensor x, torch::Tensor w, torch::Tensor qkv, torch::Tensor rstd, torch::Tensor cos_t,
                    torch::Tensor sin_t, int64_t T, int64_t H, double eps) {
   const int64_t C = w.size(1);
   TORCH_CHECK(w.size(0) == 3 * C && C == H * 128 && (3 * C) % 256 == 0, "gemm_qkv_rope: shape");
-  TORCH_CHECK(cos_t.scalar_type() == at::kFloat && cos_t.is_contiguous() && cos_t.size(1) == 64 &&
-                  sin_t.is_contiguous() && cos_t.size(0) >= T, "gemm_qkv_rope: rope tables");
+  TORCH_CHECK(cos_t.scalar_type() == at::kFloat && sin_t.scalar_type() == at::kFloat && cos_t.is_contiguous() &&
+                  sin_t.is_contiguous() && cos_t.size(0) == 64 && cos_t.sizes() == sin_t.sizes() &&
+                  cos_t.size(1) >= T, "gemm_qkv_rope: transposed rope tables (64, >= T)");
   TORCH_CHECK(rstd.scalar_type() == at::kFloat && rstd.numel() >= x.size(0) * 2 * H, "gemm_qkv_rope: rstd");
   GemmArgs r{};
   r.rope_cos = cos_t.data_ptr<float>();
   r.rope_sin = sin_t.data_ptr<float>();
   r.rope_rstd = rstd.data_ptr<float>();
-  r.rope_T = int(T); r.rope_H = int(H); r.rope_C = int(C); r.rope_eps = float(eps);
+  r.rope_T = int(T); r.rope_ld = cos_t.size(1); r.rope_H = int(H); r.rope_C = int(C); r.rope_eps = float(eps);
   gemm_impl(x, false, w, false, qkv, kRopeNorm, 1.0, c10::nullopt, c10::nullopt, 1, 256, &r);
 }
 

@@ -90,6 +90,7 @@ class FusedGpt:
                              f"rows), got {self.cfg.vocab_size}; train the tokenizer with such a --vocab-size")
         cos, sin = rope_tables(self.cfg, store.device)
         self.cos, self.sin = cos.contiguous(), sin.contiguous()
+        self.cos_t, self.sin_t = self.cos.t().contiguous(), self.sin.t().contiguous()  # QKV epilogue layout
         self._ws: Dict[Tuple[int, int, bool], _Workspace] = {}
         # RoPE + QK-norm live in the QKV GEMM epilogue (forward) and in the
         # attention backward's dQ/dK write-out when the shapes allow it.
@@ -121,7 +122,7 @@ class FusedGpt:
             p = f"blocks.{i}."
             h1 = L.rmsnorm(x, eps, out=ws.h1[j], rstd=ws.rstd1[j])
             if self.fuse_rope:
-                qkv = gemm.linear_qkv_rope(h1, st.qkv_work(i), ws.qkv[j], ws.rstd_qk[j], self.cos, self.sin, t,
+                qkv = gemm.linear_qkv_rope(h1, st.qkv_work(i), ws.qkv[j], ws.rstd_qk[j], self.cos_t, self.sin_t, t,
                                            cfg.n_head, eps)
             else:
                 qkv = gemm.linear(h1, st.qkv_work(i), out=ws.qkv[j])

@@ -68,11 +68,13 @@ def qkv_rope_supported(n_embd: int, head_dim: int) -> bool:
     return head_dim == 128 and (3 * n_embd) % 256 == 0
 
 
-def linear_qkv_rope(x, w_qkv, out, rstd, cos, sin, seq_len: int, n_head: int, eps: float):
+def linear_qkv_rope(x, w_qkv, out, rstd, cos_t, sin_t, seq_len: int, n_head: int, eps: float):
     """out = x w_qkv^T with RoPE (positions row % seq_len) and RMSNorm over each
     q/k head fused into the GEMM epilogue; 1/denominator per (row, q|k, head)
-    goes to rstd (the layout the RoPE backward reads)."""
-    ext().gemm_qkv_rope(x, w_qkv, out, rstd, cos, sin, seq_len, n_head, eps)
+    goes to rstd (the layout the RoPE backward reads). ``cos_t``/``sin_t`` are
+    the (positions, 64) RoPE tables transposed to (64, positions), contiguous,
+    so the epilogue's per-row table reads are coalesced."""
+    ext().gemm_qkv_rope(x, w_qkv, out, rstd, cos_t, sin_t, seq_len, n_head, eps)
     return out
 
 

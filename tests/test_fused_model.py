@@ -68,6 +68,6 @@ def test_qkv_gemm_with_fused_rope_matches_separate_kernels():
     L.rope_qknorm(ref, r1, cos, sin, 256, 2, 1e-6)
     out = torch.empty_like(ref)
     r2 = torch.empty_like(r1)
-    gemm.linear_qkv_rope(x, w, out, r2, cos, sin, 256, 2, 1e-6)
+    gemm.linear_qkv_rope(x, w, out, r2, cos.t().contiguous(), sin.t().contiguous(), 256, 2, 1e-6)
     assert (out.float() - ref.float()).abs().max().item() < 3e-2
     assert (r1 - r2).abs().max().item() < 1e-3 * r1.abs().max().item()
