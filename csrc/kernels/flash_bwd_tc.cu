@@ -282,6 +282,19 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
         // pairs (i, i + 64). Columns are processed 32 + 32 at a time.
         const long row = long(b) * a.T + key;
         const __nv_bfloat16* yk = a.qkv + row * 3 * a.C + a.C + h * HD;
+        // Each lane reads its own row of y and of the RoPE tables: 16-byte
+        // vector loads (8 bf16 / 4 fp32) keep the warp's cache-line requests
+        // per column few.
+        auto load8 = [](const __nv_bfloat16* p, float (&v)[8]) {
+          const uint4 w = *reinterpret_cast<const uint4*>(p);
+          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f = unpack_bf16x2(ws[k]);
+            v[2 * k] = f.x;
+            v[2 * k + 1] = f.y;
+          }
+        };
         float dot = 0.f, r = 0.f;
         if (a.rope_rstd) {
           r = a.rope_rstd[row * 2 * a.H + a.H + h];
@@ -290,31 +303,48 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
             float x[32];
             tmem_ld_32x32(tmem + lanes + 256 + c * 32, x);
 #pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-              const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(yk + c * 32 + i));
-              dot += f.x * x[i] + f.y * x[i + 1];
+            for (int u = 0; u < 4; ++u) {
+              float y[8];
+              load8(yk + c * 32 + u * 8, y);
+#pragma unroll
+              for (int k = 0; k < 8; ++k) dot += y[k] * x[u * 8 + k];
             }
           }
           dot *= a.scale / float(HD);
         }
+        const float* crow = a.rope_rstd ? a.rope_cos + long(key) * 64 : nullptr;
+        const float* srow = a.rope_rstd ? a.rope_sin + long(key) * 64 : nullptr;
 #pragma unroll 1
         for (int c = 0; c < 2; ++c) {
           float x1[32], x2[32];
           tmem_ld_32x32(tmem + lanes + 256 + c * 32, x1);
           tmem_ld_32x32(tmem + lanes + 256 + (c + 2) * 32, x2);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            float g1 = x1[i] * a.scale, g2 = x2[i] * a.scale;
+          for (int u = 0; u < 4; ++u) {
+            float y1[8], y2[8], cs[8], sn[8];
             if (a.rope_rstd) {
-              const int col = c * 32 + i;
-              const float y1 = __bfloat162float(yk[col]), y2 = __bfloat162float(yk[col + 64]);
-              const float d1 = r * (g1 - y1 * dot), d2 = r * (g2 - y2 * dot);
-              const float cs = __ldg(a.rope_cos + long(key) * 64 + col), sn = __ldg(a.rope_sin + long(key) * 64 + col);
-              g1 = d1 * cs - d2 * sn;  // dx1 = dy1 cos - dy2 sin
-              g2 = d1 * sn + d2 * cs;  // dx2 = dy1 sin + dy2 cos
+              load8(yk + c * 32 + u * 8, y1);
+              load8(yk + 64 + c * 32 + u * 8, y2);
+#pragma unroll
+              for (int k = 0; k < 8; k += 4) {
+                const float4 c4 = __ldg(reinterpret_cast<const float4*>(crow + c * 32 + u * 8 + k));
+                const float4 s4 = __ldg(reinterpret_cast<const float4*>(srow + c * 32 + u * 8 + k));
+                cs[k] = c4.x; cs[k + 1] = c4.y; cs[k + 2] = c4.z; cs[k + 3] = c4.w;
+                sn[k] = s4.x; sn[k + 1] = s4.y; sn[k + 2] = s4.z; sn[k + 3] = s4.w;
+              }
             }
-            x1[i] = g1;
-            x2[i] = g2;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const int i = u * 8 + k;
+              float g1 = x1[i] * a.scale, g2 = x2[i] * a.scale;
+              if (a.rope_rstd) {
+                const float d1 = r * (g1 - y1[k] * dot), d2 = r * (g2 - y2[k] * dot);
+                g1 = d1 * cs[k] - d2 * sn[k];  // dx1 = dy1 cos - dy2 sin
+                g2 = d1 * sn[k] + d2 * cs[k];  // dx2 = dy1 sin + dy2 cos
+              }
+              x1[i] = g1;
+              x2[i] = g2;
+            }
           }
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
@@ -510,8 +540,11 @@ void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torc
   a.err = error_word();
   if (const char* d = std::getenv("NANOGPT_FB_DEBUG")) a.dbg = std::atoi(d);
   if (rope_rstd.has_value()) {
-    TORCH_CHECK(rope_cos.has_value() && rope_sin.has_value() && rope_cos->size(1) == 64 && rope_cos->size(0) >= T,
-                "flash_bwd_tc: rope tables");
+    TORCH_CHECK(rope_cos.has_value() && rope_sin.has_value() && rope_cos->size(1) == 64 && rope_cos->size(0) >= T &&
+                    rope_cos->is_contiguous() && rope_sin->is_contiguous() &&
+                    reinterpret_cast<uintptr_t>(rope_cos->data_ptr()) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(rope_sin->data_ptr()) % 16 == 0,
+                "flash_bwd_tc: rope tables (T, 64), contiguous, 16-byte aligned");
     a.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
     a.rope_rstd = rope_rstd->data_ptr<float>();
     a.rope_cos = rope_cos->data_ptr<float>();
