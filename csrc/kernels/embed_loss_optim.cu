@@ -2,7 +2,7 @@
 //   * embedding_fwd/bwd  gather fp32 master rows -> bf16 activations; scatter-add
 //                        bf16 row grads into the fp32 gradient with vector atomics
 //                        (rs-nanogpt src/model/embedding.rs:33-35, src/model/gpt.rs:103)
-//   * softmax_xent       one pass over a chunk of bf16 logits rows: fp32 log-sum-exp,
+//   * softmax_xent       two streaming passes over a chunk of bf16 logits rows: fp32 log-sum-exp,
 //                        per-row NLL with ignore_index -1, and (optionally) the
 //                        gradient (softmax - onehot) * scale written in place over
 //                        the logits (src/model/loss.rs:20-82). Together with the
@@ -111,67 +111,104 @@ __device__ __forceinline__ float block_reduce(float v, float* smem, Op op) {
 }
 
 // NV = 8-element vectors held in registers per thread (NV * 8 * 512 >= V).
-template <int NV>
-__global__ void __launch_bounds__(kXentThreads) softmax_xent_kernel(
+// Online softmax statistics: the running max m and sum s = sum exp(v - m).
+__device__ __forceinline__ void xent_absorb8(uint4 w, float& m, float& s) {
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+  float f[8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 p = unpack_bf16x2(ws[j]);
+    f[2 * j] = p.x;
+    f[2 * j + 1] = p.y;
+  }
+  float cm = f[0];
+#pragma unroll
+  for (int j = 1; j < 8; ++j) cm = fmaxf(cm, f[j]);
+  if (cm > m) {
+    s *= __expf(m - cm);  // m = -inf on the first chunk: s is 0 and stays 0
+    m = cm;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s += __expf(f[j] - m);
+}
+
+__device__ __forceinline__ void xent_merge(float& m, float& s, float m2, float s2) {
+  const float mm = fmaxf(m, m2);
+  if (mm == -INFINITY) return;
+  s = (m == -INFINITY ? 0.f : s * __expf(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - mm));
+  m = mm;
+}
+
+// One CTA per row, streaming: pass 1 reads the row once for the online max /
+// sum, pass 2 reads it again (an L2 hit: the rows in flight on the GPU, about
+// 4 per SM x 128 KB, fit in L2) and writes the gradient in place. No row is
+// held in registers, so several rows share an SM and hide each other's latency.
+__global__ void __launch_bounds__(kXentThreads, 4) softmax_xent_kernel(
     __nv_bfloat16* logits, long ld, const int64_t* __restrict__ targets, float* __restrict__ nll_out, int V,
     float grad_scale, bool write_grad) {
-  __shared__ float red[kXentThreads / 32];
+  __shared__ float red_m[kXentThreads / 32], red_s[kXentThreads / 32];
+  __shared__ float bc[2];
   const int row = blockIdx.x;
   __nv_bfloat16* lr = logits + long(row) * ld;
-  uint4 reg[NV];
-  float mx = -INFINITY;
+  constexpr int kStep = kXentThreads * 8;
+  float m = -INFINITY, s = 0.f;
+  int c = threadIdx.x * 8;
+  for (; c + 3 * kStep < V; c += 4 * kStep) {
+    uint4 w[4];
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int c = (i * kXentThreads + threadIdx.x) * 8;
-    if (c < V) {
-      reg[i] = *reinterpret_cast<const uint4*>(lr + c);
-      uint32_t w[4] = {reg[i].x, reg[i].y, reg[i].z, reg[i].w};
+    for (int k = 0; k < 4; ++k) w[k] = *reinterpret_cast<const uint4*>(lr + c + k * kStep);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float2 f = unpack_bf16x2(w[j]);
-        mx = fmaxf(mx, fmaxf(f.x, f.y));
-      }
-    }
+    for (int k = 0; k < 4; ++k) xent_absorb8(w[k], m, s);
   }
-  mx = block_reduce(mx, red, [](float a, float b) { return fmaxf(a, b); });
-  float se = 0.f;
+  for (; c < V; c += kStep) xent_absorb8(*reinterpret_cast<const uint4*>(lr + c), m, s);
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int c = (i * kXentThreads + threadIdx.x) * 8;
-    if (c < V) {
-      uint32_t w[4] = {reg[i].x, reg[i].y, reg[i].z, reg[i].w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float2 f = unpack_bf16x2(w[j]);
-        se += __expf(f.x - mx) + __expf(f.y - mx);
-      }
-    }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    xent_merge(m, s, m2, s2);
   }
-  se = block_reduce(se, red, [](float a, float b) { return a + b; });
-  const float lse = mx + __logf(se);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  if (lane == 0) { red_m[warp] = m; red_s[warp] = s; }
+  __syncthreads();
+  if (warp == 0) {
+    m = lane < kXentThreads / 32 ? red_m[lane] : -INFINITY;
+    s = lane < kXentThreads / 32 ? red_s[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      xent_merge(m, s, m2, s2);
+    }
+    if (lane == 0) { bc[0] = m; bc[1] = s; }
+  }
+  __syncthreads();
+  const float lse = bc[0] + __logf(bc[1]);
   const int64_t t = targets[row];
   const bool valid = t >= 0 && t < V;
   if (threadIdx.x == 0 && nll_out) nll_out[row] = valid ? lse - __bfloat162float(lr[t]) : 0.f;
   if (!write_grad) return;
   __syncthreads();  // lr[t] read above before it is overwritten
-  const float s = valid ? grad_scale : 0.f;
+  const float sc = valid ? grad_scale : 0.f;
+  auto grad8 = [&](uint4 w, int col0) {
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    uint32_t o[4];
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int c = (i * kXentThreads + threadIdx.x) * 8;
-    if (c < V) {
-      uint32_t w[4] = {reg[i].x, reg[i].y, reg[i].z, reg[i].w};
-      uint32_t o[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float2 f = unpack_bf16x2(w[j]);
-        const int col = c + 2 * j;
-        float g0 = __expf(f.x - lse) - (col == t ? 1.f : 0.f);
-        float g1 = __expf(f.y - lse) - (col + 1 == t ? 1.f : 0.f);
-        o[j] = pack_bf16x2(g0 * s, g1 * s);
-      }
-      *reinterpret_cast<uint4*>(lr + c) = make_uint4(o[0], o[1], o[2], o[3]);
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(ws[j]);
+      const int col = col0 + 2 * j;
+      const float g0 = __expf(f.x - lse) - (col == t ? 1.f : 0.f);
+      const float g1 = __expf(f.y - lse) - (col + 1 == t ? 1.f : 0.f);
+      o[j] = pack_bf16x2(g0 * sc, g1 * sc);
     }
+    *reinterpret_cast<uint4*>(lr + col0) = make_uint4(o[0], o[1], o[2], o[3]);
+  };
+  c = threadIdx.x * 8;
+  for (; c + 3 * kStep < V; c += 4 * kStep) {
+    uint4 w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) w[k] = *reinterpret_cast<const uint4*>(lr + c + k * kStep);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) grad8(w[k], c + k * kStep);
   }
+  for (; c < V; c += kStep) grad8(*reinterpret_cast<const uint4*>(lr + c), c);
 }
 
 // logits: (rows, V) bf16 chunk; targets: (rows,) int64 with -1 = ignore.
@@ -191,17 +228,8 @@ void softmax_xent(torch::Tensor logits, torch::Tensor targets, c10::optional<tor
   const at::cuda::CUDAGuard guard(logits.device());
   auto stream = at::cuda::getCurrentCUDAStream();
   auto lp = reinterpret_cast<__nv_bfloat16*>(logits.data_ptr());
-  const int per = kXentThreads * 8;
-  const int nv = (V + per - 1) / per;
-#define XENT(N) softmax_xent_kernel<N><<<rows, kXentThreads, 0, stream>>>(lp, logits.stride(0), \
-      targets.data_ptr<int64_t>(), np, V, float(grad_scale), write_grad)
-  if (nv <= 1) XENT(1);
-  else if (nv <= 2) XENT(2);
-  else if (nv <= 4) XENT(4);
-  else if (nv <= 8) XENT(8);
-  else if (nv <= 16) XENT(16);
-  else TORCH_CHECK(false, "xent: vocab above 65536 is not supported");
-#undef XENT
+  softmax_xent_kernel<<<rows, kXentThreads, 0, stream>>>(lp, logits.stride(0), targets.data_ptr<int64_t>(), np, V,
+                                                        float(grad_scale), write_grad);
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "softmax_xent launch failed");
 }
 
