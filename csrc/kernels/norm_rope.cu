@@ -70,7 +70,7 @@ __global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfl
     if (c < C) {
       float o[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = v[i][j] / denom;
+      for (int j = 0; j < 8; ++j) o[j] = v[i][j] * r;  // within 1 fp32 ulp of v / denom
       store8(yr + c, o);
     }
   }
