@@ -160,6 +160,8 @@ def linear_wgrad(dy, x, grad, alpha: float = 1.0, splits: int = 0):
     if splits <= 0:
         tiles = ((n + 127) // 128) * ((k + bn - 1) // bn)
         k_blocks = (dy.shape[0] + 63) // 64
-        splits = max(1, min(k_blocks // 8, (8 * _sms() + tiles - 1) // tiles))
+        # About 8 units per SM, and at least 8 splits: measured 5-6 % faster than
+        # 6 splits on the 1280x5120 / 5120x1280 weight gradients of d20.
+        splits = max(1, min(k_blocks // 8, max(8, (8 * _sms() + tiles - 1) // tiles)))
     ext().gemm(dy, True, x, True, grad, ATOMIC_F32, alpha, None, None, splits, bn)
     return grad
