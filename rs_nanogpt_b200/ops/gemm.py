@@ -8,6 +8,8 @@ copies are ever made:
 * ``linear_dgrad(dy, w)``     dx = dy w         (w is MN-major)
 * ``linear_wgrad(dy, x, g)``  g += dy^T x       (both MN-major, split-K, fp32 atomics)
 """
+import os
+
 import torch
 
 from ._ext import ext
@@ -149,6 +151,9 @@ def linear_qkv_decode(x, w_qkv, acc, qkv, k_cache, v_cache, pos, cos, sin, n_hea
     return qkv
 
 
+_WGRAD_UNITS = int(os.environ.get("NANOGPT_WGRAD_UNITS", "8"))
+
+
 def linear_wgrad(dy, x, grad, alpha: float = 1.0, splits: int = 0):
     """grad[N,K] (fp32) += alpha * dy[M,N]^T @ x[M,K].
 
@@ -160,8 +165,9 @@ def linear_wgrad(dy, x, grad, alpha: float = 1.0, splits: int = 0):
     if splits <= 0:
         tiles = ((n + 127) // 128) * ((k + bn - 1) // bn)
         k_blocks = (dy.shape[0] + 63) // 64
-        # About 8 units per SM, and at least 8 splits: measured 5-6 % faster than
-        # 6 splits on the 1280x5120 / 5120x1280 weight gradients of d20.
-        splits = max(1, min(k_blocks // 8, max(8, (8 * _sms() + tiles - 1) // tiles)))
+        # About _WGRAD_UNITS work units per SM (8; 4 and 2 measured the same per
+        # training micro-batch). A floor of 8 splits was 5 % faster in isolation
+        # but 3 % slower per micro-batch, so split counts are judged in the step.
+        splits = max(1, min(k_blocks // 8, (_WGRAD_UNITS * _sms() + tiles - 1) // tiles))
     ext().gemm(dy, True, x, True, grad, ATOMIC_F32, alpha, None, None, splits, bn)
     return grad
