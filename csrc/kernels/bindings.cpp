@@ -26,7 +26,7 @@ void flash_bwd(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch::
 void ddp_barrier(int64_t pads_dev, int64_t rank, int64_t world, int64_t epoch);
 void ddp_rs_adam_ag(int64_t grads_dev, int64_t works_dev, int64_t world, torch::Tensor master, torch::Tensor m,
                     torch::Tensor v, int64_t shard_lo, int64_t shard_hi, torch::Tensor groups, double grad_scale,
-                    c10::optional<torch::Tensor> sumsq);
+                    c10::optional<torch::Tensor> sumsq, int64_t mv_base);
 void flash_fwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor lse, int64_t B, int64_t T, int64_t H);
 bool flash_fwd_tc_supported(int64_t T, int64_t HD);
 void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch::Tensor lse, torch::Tensor dsum,

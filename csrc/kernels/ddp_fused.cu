@@ -67,9 +67,10 @@ struct DdpArgs {
   const float* const* grads;      // [world] peer gradient buffers
   __nv_bfloat16* const* works;    // [world] peer bf16 working-copy buffers
   float* master;
-  float* m;
-  float* v;
+  float* m;                       // AdamW moments of this rank's shard only:
+  float* v;                       //   element i lives at m[i - mv_base]
   long shard_lo, shard_hi;        // this rank's elements, multiples of 4
+  long mv_base;
   DdpGroup groups[3];
   int ngroups, world;
   float grad_scale;               // multiplies the summed gradient (includes 1/world)
@@ -95,8 +96,10 @@ __global__ void __launch_bounds__(256) ddp_rs_adam_ag_kernel(const DdpArgs a) {
     const DdpGroup& G = a.groups[gi];
     const bool in_group = i >= G.lo && i < G.hi;  // padding between groups stays untouched
     float4 pp = *reinterpret_cast<float4*>(a.master + i);
-    float4 mm = *reinterpret_cast<float4*>(a.m + i);
-    float4 vv = *reinterpret_cast<float4*>(a.v + i);
+    float* const mp = a.m + (i - a.mv_base);
+    float* const vp = a.v + (i - a.mv_base);
+    float4 mm = *reinterpret_cast<float4*>(mp);
+    float4 vv = *reinterpret_cast<float4*>(vp);
     float* P = &pp.x;
     float* M = &mm.x;
     float* V = &vv.x;
@@ -110,8 +113,8 @@ __global__ void __launch_bounds__(256) ddp_rs_adam_ag_kernel(const DdpArgs a) {
         P[j] = P[j] * decay - ((M[j] * G.scale_m) / (sqrtf(V[j] * G.scale_v) + G.eps)) * G.lr;
       }
       *reinterpret_cast<float4*>(a.master + i) = pp;
-      *reinterpret_cast<float4*>(a.m + i) = mm;
-      *reinterpret_cast<float4*>(a.v + i) = vv;
+      *reinterpret_cast<float4*>(mp) = mm;
+      *reinterpret_cast<float4*>(vp) = vv;
     }
     const uint2 w = make_uint2(pack_bf16x2(pp.x, pp.y), pack_bf16x2(pp.z, pp.w));
 #pragma unroll
@@ -138,14 +141,21 @@ void ddp_barrier(int64_t pads_dev, int64_t rank, int64_t world, int64_t epoch) {
 }
 
 // groups: (n_groups, 9) float64 rows [lo, hi, lr, b1, b2, eps, wd, scale_m, scale_v]
+// m, v: the moments of elements [mv_base, mv_base + m.numel()) (a shard-sized
+// slice, or the whole buffer with mv_base 0).
 void ddp_rs_adam_ag(int64_t grads_dev, int64_t works_dev, int64_t world, torch::Tensor master, torch::Tensor m,
                     torch::Tensor v, int64_t shard_lo, int64_t shard_hi, torch::Tensor groups, double grad_scale,
-                    c10::optional<torch::Tensor> sumsq) {
+                    c10::optional<torch::Tensor> sumsq, int64_t mv_base) {
   TORCH_CHECK(world >= 1 && world <= kMaxWorld, "ddp: world size 1..8");
   TORCH_CHECK(master.scalar_type() == at::kFloat && m.scalar_type() == at::kFloat && v.scalar_type() == at::kFloat,
               "ddp: fp32 state");
   TORCH_CHECK(shard_lo % 4 == 0 && shard_hi % 4 == 0 && shard_lo <= shard_hi && shard_hi <= master.numel(),
               "ddp: shard bounds must be multiples of 4 inside the buffer");
+  TORCH_CHECK(m.numel() == v.numel() && m.is_contiguous() && v.is_contiguous() && mv_base % 4 == 0 &&
+                  shard_lo >= mv_base && (shard_hi - mv_base <= m.numel() || shard_hi == shard_lo),
+              "ddp: the moment slices must cover the shard");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(m.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(v.data_ptr()) % 16 == 0,
+              "ddp: moment slices must be 16-byte aligned");
   TORCH_CHECK(groups.dtype() == at::kDouble && groups.dim() == 2 && groups.size(1) == 9 && groups.size(0) <= 3,
               "ddp: groups table");
   DdpArgs a{};
@@ -156,6 +166,7 @@ void ddp_rs_adam_ag(int64_t grads_dev, int64_t works_dev, int64_t world, torch::
   a.v = v.data_ptr<float>();
   a.shard_lo = shard_lo;
   a.shard_hi = shard_hi;
+  a.mv_base = mv_base;
   a.world = int(world);
   a.grad_scale = float(grad_scale);
   auto g = groups.accessor<double, 2>();

@@ -597,7 +597,8 @@ extern "C" __attribute__((visibility("default"))) const char* nanogpt_noalloc_er
     case NANOGPT_NOALLOC_ERR_TOO_LARGE:
       return "batch * n_head * seq_len exceeds the fixed scratch of NANOGPT_NOALLOC_MAX_ROWS (1048576) floats";
     case NANOGPT_NOALLOC_ERR_BAD_ARG:
-      return "invalid argument (null or unaligned pointer, head_dim not 64/128, or non-positive size)";
+      return "invalid argument (null or unaligned pointer, head_dim not 64/128, non-positive size, or "
+             "batch * n_head above 65535)";
     case NANOGPT_NOALLOC_ERR_CUDA: return "a CUDA runtime call failed (see cudaGetLastError)";
     default: return "unknown error code";
   }
@@ -613,6 +614,8 @@ extern "C" __attribute__((visibility("default"))) int nanogpt_flash_attention_bw
     return NANOGPT_NOALLOC_ERR_BAD_ARG;
   const size_t rows = size_t(batch) * size_t(n_head) * size_t(seq_len);
   if (rows > NANOGPT_NOALLOC_MAX_ROWS) return NANOGPT_NOALLOC_ERR_TOO_LARGE;
+  // The kernels put (batch, head) pairs on grid.y, which holds at most 65535.
+  if (size_t(batch) * size_t(n_head) > NANOGPT_NOALLOC_MAX_BATCH_HEADS) return NANOGPT_NOALLOC_ERR_BAD_ARG;
 
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return NANOGPT_NOALLOC_ERR_CUDA;
@@ -657,25 +660,31 @@ extern "C" __attribute__((visibility("default"))) int nanogpt_flash_attention_bw
   const long items = long(batch) * seq_len * n_head;
   dim3 gq(unsigned((seq_len + 127) / 128), unsigned(batch * n_head));
   dim3 gk(unsigned((seq_len + 63) / 64), unsigned(batch * n_head));
+  // An error left pending by earlier, unrelated work is reported without
+  // being cleared, before anything is queued, so it is not mistaken for (or
+  // hidden by) a failure of this call.
+  if (cudaPeekAtLastError() != cudaSuccess) return NANOGPT_NOALLOC_ERR_CUDA;
+  const int smq = (2 * 128 + 4 * 64) * head_dim * 2, smk = (2 * 64 + 4 * 32) * head_dim * 2 + 4 * 32 * 4;
   cudaError_t e = cudaSuccess;
   if (head_dim == 128) {
-    const int smq = (2 * 128 + 4 * 64) * 128 * 2, smk = (2 * 64 + 4 * 32) * 128 * 2 + 4 * 32 * 4;
     e = cudaFuncSetAttribute(flash_bwd_dq_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smq);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(flash_bwd_dkv_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smk);
-    if (e != cudaSuccess) return NANOGPT_NOALLOC_ERR_CUDA;
-    flash_bwd_dot_kernel<128><<<unsigned((items + 7) / 8), 256, 0, stream>>>(d);
-    flash_bwd_dq_kernel<128><<<gq, 256, smq, stream>>>(q);
-    flash_bwd_dkv_kernel<128><<<gk, 128, smk, stream>>>(kv);
   } else {
-    const int smq = (2 * 128 + 4 * 64) * 64 * 2, smk = (2 * 64 + 4 * 32) * 64 * 2 + 4 * 32 * 4;
     e = cudaFuncSetAttribute(flash_bwd_dq_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smq);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(flash_bwd_dkv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smk);
-    if (e != cudaSuccess) return NANOGPT_NOALLOC_ERR_CUDA;
-    flash_bwd_dot_kernel<64><<<unsigned((items + 7) / 8), 256, 0, stream>>>(d);
-    flash_bwd_dq_kernel<64><<<gq, 256, smq, stream>>>(q);
-    flash_bwd_dkv_kernel<64><<<gk, 128, smk, stream>>>(kv);
   }
+  if (e != cudaSuccess) return NANOGPT_NOALLOC_ERR_CUDA;
+  // Each launch is checked on its own; a failed launch stops the sequence, so
+  // a later kernel never consumes the output of one that did not run.
+  if (head_dim == 128) flash_bwd_dot_kernel<128><<<unsigned((items + 7) / 8), 256, 0, stream>>>(d);
+  else flash_bwd_dot_kernel<64><<<unsigned((items + 7) / 8), 256, 0, stream>>>(d);
+  if (cudaGetLastError() != cudaSuccess) return NANOGPT_NOALLOC_ERR_CUDA;
+  if (head_dim == 128) flash_bwd_dq_kernel<128><<<gq, 256, smq, stream>>>(q);
+  else flash_bwd_dq_kernel<64><<<gq, 256, smq, stream>>>(q);
+  if (cudaGetLastError() != cudaSuccess) return NANOGPT_NOALLOC_ERR_CUDA;
+  if (head_dim == 128) flash_bwd_dkv_kernel<128><<<gk, 128, smk, stream>>>(kv);
+  else flash_bwd_dkv_kernel<64><<<gk, 128, smk, stream>>>(kv);
   return cudaGetLastError() == cudaSuccess ? NANOGPT_NOALLOC_OK : NANOGPT_NOALLOC_ERR_CUDA;
 }

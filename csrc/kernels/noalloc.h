@@ -25,8 +25,13 @@
 //    Each call overwrites every entry it reads, so nothing must start at zero,
 //    but calls whose GPU work overlaps (different streams without ordering, or
 //    different host threads) race on it and must not be issued.
-//  * Inputs and outputs are supplied by the caller; head_dim must be 64 or 128
-//    and all pointers 16-byte aligned.
+//  * Inputs and outputs are supplied by the caller; head_dim must be 64 or 128,
+//    all pointers 16-byte aligned, and batch * n_head at most
+//    NANOGPT_NOALLOC_MAX_BATCH_HEADS (65535, the grid.y limit).
+//  * A CUDA error already pending when the call starts (from earlier work) is
+//    returned as NANOGPT_NOALLOC_ERR_CUDA without clearing it and before
+//    anything is queued; each of the three launches is checked on its own and
+//    a failed launch stops the sequence.
 #pragma once
 #include <cuda_runtime.h>
 
@@ -35,6 +40,7 @@ extern "C" {
 #endif
 
 #define NANOGPT_NOALLOC_MAX_ROWS (1u << 20)
+#define NANOGPT_NOALLOC_MAX_BATCH_HEADS 65535u
 
 #define NANOGPT_NOALLOC_OK 0
 #define NANOGPT_NOALLOC_ERR_TOO_LARGE 1

@@ -99,7 +99,7 @@ def main(argv=None):
         def fused():
             barrier()
             ext().ddp_rs_adam_ag(int(hg.buffer_ptrs_dev), int(hw.buffer_ptrs_dev), world, master, m, v, lo, hi,
-                                 groups, 1.0 / world, None)
+                                 groups, 1.0 / world, None, 0)
             barrier()
 
         g_ar = torch.randn(n, device=dev)

@@ -79,8 +79,9 @@ def run_chat(args) -> None:
     meta = checkpoint.load_meta(args.checkpoint)
     tok = BpeTokenizer.from_file(args.vocab)
     if tok.vocab_size() != meta.config.vocab_size:
-        raise ValueError(f"vocab {args.vocab} has {tok.vocab_size()} tokens but the checkpoint was trained with "
-                         f"{meta.config.vocab_size}; a mismatched vocabulary loads fine and scores garbage")
+        raise ValueError(f"vocabulary size mismatch: {args.vocab} defines {tok.vocab_size()} tokens, the "
+                         f"checkpoint expects {meta.config.vocab_size}. Pass the vocab file the checkpoint was "
+                         "trained with")
     store, _ = checkpoint.load(args.checkpoint, device)
     model = cached_model(store)
     print(f"chat: {args.checkpoint} | step {meta.step} | val_bpb {meta.val_bpb:.4f} | context "

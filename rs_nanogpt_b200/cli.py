@@ -136,7 +136,11 @@ def _add_extensions(p: argparse.ArgumentParser) -> None:
     p.add_argument("--device", default=None, help="cuda or cpu (default: cuda when available)")
     p.add_argument("--init", choices=["reference", "bench"], default="reference",
                    help="weight init (pretrain only): the reference's, or N(0,0.02) with zero projections")
-    p.add_argument("--save-optimizer", action="store_true", help="also save AdamW state with best/ (resume)")
+    p.add_argument("--save-optimizer", action="store_true",
+                   help="also save the AdamW state (optim.pt) with best/, so that --resume can continue from it")
+    p.add_argument("--resume", default=None, metavar="DIR",
+                   help="continue from a checkpoint saved with --save-optimizer: its weights, AdamW state and "
+                        "step (the data stream starts over; the reference has no resume)")
 
 
 # ---- validation -----------------------------------------------------------------------

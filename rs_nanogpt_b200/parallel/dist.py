@@ -122,6 +122,17 @@ class DistCtx:
             dist.all_reduce(chunk, op=dist.ReduceOp.SUM)
             chunk.mul_(inv)
 
+    def align_streams(self) -> None:
+        """A one-element all-reduce on the current stream: work enqueued after
+        it on any rank starts only once every rank has reached this point on
+        the device. The host does not wait."""
+        if self._world == 1:
+            return
+        import torch.distributed as dist
+        if getattr(self, "_align", None) is None:
+            self._align = torch.zeros(1, dtype=torch.float32, device=self._comm_device())
+        dist.all_reduce(self._align)
+
     def broadcast_params(self, flat: torch.Tensor) -> None:
         if self._world == 1:
             return

@@ -15,9 +15,12 @@ kernels on the compute stream (``csrc/kernels/ddp_fused.cu``):
    its weights, so the next step may start.
 
 Mathematically this is DDP (gradient mean) followed by the reference's AdamW;
-only the summation order differs. The fp32 master weights and AdamW moments
-are sharded (each rank updates only its slice); ``gather_master`` rebuilds the
-full fp32 master when a checkpoint or a sample needs it.
+only the summation order differs. The AdamW moments exist only for this rank's
+shards (ZeRO-1: a rank holds 2 x 4 bytes per parameter / world of optimizer
+state); the fp32 master is updated only on the shard, and ``gather_master``
+rebuilds the full master when a checkpoint or a sample needs it.
+``gather_optimizer`` / ``load_optimizer`` convert the sharded moments to and
+from the full flat layout of a checkpoint's ``optim.pt``.
 """
 from typing import Optional
 
@@ -81,6 +84,14 @@ class FusedDdp:
             sh = ((hi - lo + self.world - 1) // self.world + SHARD_ALIGN - 1) // SHARD_ALIGN * SHARD_ALIGN
             s_lo = min(hi, lo + self.rank * sh)
             self.shards[key] = (s_lo, min(hi, s_lo + sh), sh)
+        # Compact moment buffers: bucket `key`'s shard lives at
+        # [mv_off[key], mv_off[key] + shard size).
+        self.mv_off, off = {}, 0
+        for key in self.bucket_ids:
+            self.mv_off[key] = off
+            off += self.shards[key][2]
+        self.m = torch.zeros(off, dtype=torch.float32, device=dev)
+        self.v = torch.zeros(off, dtype=torch.float32, device=dev)
         self.comm_stream = torch.cuda.Stream(device=dev)
         self._groups_t = None
         self._grad_scale = 1.0
@@ -101,11 +112,12 @@ class FusedDdp:
         return torch.tensor(rows, dtype=torch.float64)
 
     def _bucket_kernel(self, key) -> None:
-        lo, hi, _ = self.shards[key]
+        lo, hi, sh = self.shards[key]
         if hi > lo:
+            o = self.mv_off[key]
             ext().ddp_rs_adam_ag(int(self.h_grad.buffer_ptrs_dev), int(self.h_work.buffer_ptrs_dev), self.world,
-                                 self.store.master, self.opt.m, self.opt.v, lo, hi, self._groups_t,
-                                 self._grad_scale / self.world, self.sumsq)
+                                 self.store.master, self.m[o:o + sh], self.v[o:o + sh], lo, hi, self._groups_t,
+                                 self._grad_scale / self.world, self.sumsq, lo)
 
     # -- one optimizer step ---------------------------------------------------------
 
@@ -146,15 +158,53 @@ class FusedDdp:
         """Norm of the reduced (mean) gradient of the last step, over all shards."""
         return self.dist.all_reduce_sums([float(self.sumsq.item())])[0] ** 0.5
 
+    def _gather(self, key, mine: torch.Tensor, dst: torch.Tensor) -> None:
+        """All-gather the shard-sized `mine` of bucket `key` from every rank
+        into the bucket's range of the flat `dst`."""
+        import torch.distributed as td
+        lo, hi = self.buckets[key]
+        sh = self.shards[key][2]
+        full = torch.empty(sh * self.world, dtype=torch.float32, device=self.store.device)
+        td.all_gather_into_tensor(full, mine)
+        dst[lo:hi].copy_(full[: hi - lo], non_blocking=True)
+
     def gather_master(self) -> None:
         """Make every rank's fp32 master complete again (after sharded updates)."""
-        import torch.distributed as td
         st = self.store
         for key in self.bucket_ids:
-            lo, hi = self.buckets[key]
             s_lo, s_hi, sh = self.shards[key]
-            full = torch.zeros(sh * self.world, dtype=torch.float32, device=st.device)
             mine = torch.zeros(sh, dtype=torch.float32, device=st.device)
             mine[: s_hi - s_lo].copy_(st.master[s_lo:s_hi])
-            td.all_gather_into_tensor(full, mine)
-            st.master[lo:hi].copy_(full[: hi - lo])
+            self._gather(key, mine, st.master)
+
+    def gather_optimizer(self, to_host: bool = True) -> dict:
+        """Full-length AdamW moments in the flat layout (collective: call it on
+        every rank). Buckets are gathered one at a time; with ``to_host`` the
+        result lives in host memory, so no rank needs 8 bytes per parameter of
+        extra device memory."""
+        st = self.store
+        out = {}
+        for name, state in (("m", self.m), ("v", self.v)):
+            dst = torch.zeros(st.total, dtype=torch.float32, device="cpu" if to_host else st.device)
+            if to_host:
+                dst = dst.pin_memory()
+            for key in self.bucket_ids:
+                o, sh = self.mv_off[key], self.shards[key][2]
+                self._gather(key, state[o:o + sh], dst)
+            torch.cuda.synchronize(st.device)
+            out[name] = dst
+        return {"step_t": self.opt.step_t, **out}
+
+    def load_optimizer(self, sd: dict) -> None:
+        """Take this rank's shards of full-length moments (every rank passes
+        the same full state)."""
+        from ..train.optim import check_state_dict
+        check_state_dict(sd, self.store.total)
+        self.opt.step_t = int(sd["step_t"])
+        for name, state in (("m", self.m), ("v", self.v)):
+            src = sd[name]
+            for key in self.bucket_ids:
+                s_lo, s_hi, sh = self.shards[key]
+                o = self.mv_off[key]
+                state[o:o + sh].zero_()
+                state[o:o + s_hi - s_lo].copy_(src[s_lo:s_hi])

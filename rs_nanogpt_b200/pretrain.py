@@ -62,6 +62,15 @@ def run_pretrain(args, env) -> None:
         n_params = store.num_params()
         lrs = GroupLrs(args.embedding_lr, args.unembedding_lr, args.matrix_lr)
         engine = TrainEngine(store, lrs, GroupWeightDecay(), dist, comm=args.backend)
+        start_step, best_bpb = 0, float("inf")
+        if getattr(args, "resume", None):
+            from .utils.checkpoint import resume
+            meta = resume(args.resume, engine)
+            start_step, best_bpb = meta.step, meta.val_bpb
+            if start_step > args.num_iters:
+                raise ValueError(f"checkpoint step {start_step} is beyond --num-iters {args.num_iters}")
+            if dist.is_master():
+                print(f"resumed from {args.resume} at step {start_step} (val bpb {best_bpb})")
         if dist.is_master():
             dtype = "bf16" if device.type == "cuda" else "f32"
             print(f"\nmodel built on {device} | compute dtype {dtype} (fp32 masters) | {n_params} parameters")
@@ -72,7 +81,7 @@ def run_pretrain(args, env) -> None:
             run_dir = unique_run_dir(args.out, str(started))
             print(f"run dir: {run_dir}")
             write_run_json(os.path.join(run_dir, "run.json"), dict(
-                phase="pretrain", device=str(device), dtype="f32", started_at_unix=started, n_params=n_params,
+                phase="pretrain", device=str(device), dtype="bf16" if device.type == "cuda" else "f32", started_at_unix=started, n_params=n_params,
                 vocab_size=cfg.vocab_size, sequence_len=cfg.sequence_len, n_layer=cfg.n_layer, n_head=cfg.n_head,
                 n_embd=cfg.n_embd, rope_base=cfg.rope_base, norm_eps=cfg.norm_eps, num_iters=args.num_iters,
                 device_batch=args.device_batch, total_batch=args.total_batch, world_size=args.gpus,
@@ -93,7 +102,7 @@ def run_pretrain(args, env) -> None:
                          sample_every=args.sample_every, sample_tokens=args.sample_tokens,
                          sample_temperature=args.sample_temperature, sample_chat=False,
                          save_optimizer=args.save_optimizer)
-        train(engine, loader, tcfg, ev, fault=_fault_from_env(dist))
+        train(engine, loader, tcfg, ev, fault=_fault_from_env(dist), start_step=start_step, best_bpb=best_bpb)
         loader.close()
         metrics.close()
         ok = True

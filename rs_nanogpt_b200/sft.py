@@ -140,9 +140,9 @@ def val_batches(args, tok, seq_len: int, device):
                                                  args.seed), seq_len, args.seed)
     view = EpochView(epoch, 0, 1, args.device_batch, device)
     if view.num_batches() == 0:
-        raise SftError(f"the val mixture packs to {epoch.stats.rows} rows, fewer than one micro-batch of "
-                       f"--device-batch {args.device_batch}; lower --device-batch, or check that --data holds "
-                       "the test split you expect")
+        raise SftError(f"validation set too small: {epoch.stats.rows} packed rows cannot fill a single "
+                       f"micro-batch of {args.device_batch} rows (--device-batch). Use a smaller --device-batch or "
+                       "make sure --data contains the test split")
     if view.num_batches() < args.eval_steps:
         raise SftError(f"the val mixture packs to {view.num_batches()} micro-batches at --device-batch "
                        f"{args.device_batch}, fewer than --eval-steps {args.eval_steps}; lower --eval-steps to <= "
@@ -157,9 +157,9 @@ def check_packs_agree(dist: DistCtx, local: List[float]) -> None:
     w = dist.world_size()
     for name, want, got in zip(names, local, reduced):
         if got != want * w:
-            raise SftError(f"ranks disagree on the packed epoch: {name} is {want} on rank {dist.rank()} but the "
-                           f"cross-rank sum is {got}, not {want * w}. Every rank must build an identical pack "
-                           "from identical files and --seed")
+            raise SftError(f"packed SFT epoch differs between ranks: rank {dist.rank()} has {name} = {want}, "
+                           f"but summed over the {w} ranks it is {got} (expected {want * w}). All ranks need the "
+                           "same data files and the same --seed")
 
 
 def run_sft(args, env) -> None:
@@ -174,8 +174,9 @@ def run_sft(args, env) -> None:
         seq = meta.config.sequence_len
         tok = BpeTokenizer.from_file(args.vocab)
         if tok.vocab_size() != meta.config.vocab_size:
-            raise SftError(f"vocab {args.vocab} has {tok.vocab_size()} tokens but the checkpoint was trained with "
-                           f"{meta.config.vocab_size}; a mismatched vocabulary loads fine and scores garbage")
+            raise SftError(f"vocabulary size mismatch: {args.vocab} defines {tok.vocab_size()} tokens, the "
+                           f"checkpoint expects {meta.config.vocab_size}. Pass the vocab file the checkpoint was "
+                           "pretrained with (a different one would load but produce meaningless token ids)")
         accum = validate_batch_geometry(args.gpus, args.device_batch, seq, args.total_batch)
         if dist.is_master():
             print(f"sft: finetuning {args.checkpoint} | seq_len {seq} | vocab {meta.config.vocab_size} | gpus "
@@ -193,8 +194,8 @@ def run_sft(args, env) -> None:
         epoch = render_and_pack(tok, train_sources(args.data, args.mmlu_epochs, args.gsm8k_epochs), seq, args.seed)
         st = epoch.stats
         if st.scored_tokens == 0:
-            raise SftError(f"the train mixture packs {st.rows} rows but scores no tokens — every target is "
-                           "ignore_index, so there is nothing to learn from")
+            raise SftError(f"no trainable targets: all {st.rows} packed training rows have every target "
+                           "masked out (ignore_index), so no gradient can be computed")
         pad_frac = st.pad_tokens / st.total_tokens if st.total_tokens else 0.0
         scored = st.scored_tokens / st.total_tokens
         if dist.is_master():
@@ -210,14 +211,14 @@ def run_sft(args, env) -> None:
                            f"grad_accum({accum}) = {dist.world_size() * args.device_batch * accum} rows")
         num_iters = epoch_iters if args.num_iters is None else args.num_iters
         if num_iters > epoch_iters:
-            raise SftError(f"--num-iters {num_iters} exceeds the {epoch_iters} steps this epoch holds; the mixture "
-                           "is packed once and not repeated, so lower --num-iters (or drop it to train the whole "
-                           "epoch)")
+            raise SftError(f"--num-iters {num_iters} is more than the {epoch_iters} optimizer steps in one pass "
+                           "over the packed mixture (SFT runs a single epoch). Use at most that many, or omit "
+                           "--num-iters to run the full epoch")
         f = args.init_lr_frac
         lrs = GroupLrs(args.embedding_lr * f, args.unembedding_lr * f, args.matrix_lr * f)
         if dist.is_master():
             write_run_json(os.path.join(run_dir, "run.json"), dict(
-                phase="sft", device=str(device), dtype="f32", started_at_unix=started, n_params=store.num_params(),
+                phase="sft", device=str(device), dtype="bf16" if device.type == "cuda" else "f32", started_at_unix=started, n_params=store.num_params(),
                 vocab_size=meta.config.vocab_size, sequence_len=seq, n_layer=meta.config.n_layer,
                 n_head=meta.config.n_head, n_embd=meta.config.n_embd, rope_base=meta.config.rope_base,
                 norm_eps=meta.config.norm_eps, num_iters=num_iters, device_batch=args.device_batch,
@@ -242,7 +243,16 @@ def run_sft(args, env) -> None:
                          sample_every=args.sample_every, sample_tokens=args.sample_tokens,
                          sample_temperature=args.sample_temperature, sample_chat=True,
                          save_optimizer=args.save_optimizer)
-        train(engine, view, tcfg, ev)
+        start_step, best_bpb = 0, float("inf")
+        if getattr(args, "resume", None):
+            # The packed epoch is deterministic (same seed, same mixture), so a
+            # resumed run skips the micro-batches the checkpoint has consumed.
+            meta_r = checkpoint.resume(args.resume, engine)
+            start_step, best_bpb = meta_r.step, meta_r.val_bpb
+            if start_step > num_iters:
+                raise SftError(f"resume checkpoint is at step {start_step}, past this run's {num_iters} steps")
+            view.next = start_step * accum
+        train(engine, view, tcfg, ev, start_step=start_step, best_bpb=best_bpb)
         metrics.close()
         ok = True
     finally:

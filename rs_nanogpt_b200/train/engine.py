@@ -23,6 +23,10 @@ from ..parallel.dist import DistCtx
 from .optim import GroupedAdamW, GroupLrs, GroupWeightDecay
 
 
+class KernelStatusError(RuntimeError):
+    pass
+
+
 @dataclass
 class StepStats:
     nll_sum: torch.Tensor     # device scalar, fp32 (sum over this rank's tokens)
@@ -35,16 +39,21 @@ class TrainEngine:
         self.store = store
         self.cfg = store.cfg
         self.dist = dist or DistCtx.single(store.device)
-        self.opt = GroupedAdamW(store, lrs, self.cfg.n_embd, wd)
         self.comm = comm
+        fused = comm == "fused" and self.dist.world_size() > 1 and store.device.type == "cuda"
+        self.opt = GroupedAdamW(store, lrs, self.cfg.n_embd, wd, allocate_state=not fused)
         self.fused_ddp = None
+        # Reads (and clears) the kernels' device error word; None on CPU.
+        self.status_fn = None
         if store.device.type == "cuda":
+            from ..ops._ext import kernel_status
+            self.status_fn = kernel_status
             from ..models.fused import FusedGpt
             self.model = FusedGpt(store)
         else:
             from ..models.reference import ReferenceGpt
             self.model = ReferenceGpt(store, torch.float32)
-        if comm == "fused" and self.dist.world_size() > 1 and store.device.type == "cuda":
+        if fused:
             from ..parallel.fused_ddp import FusedDdp
             self.fused_ddp = FusedDdp(store, self.opt, self.dist)
 
@@ -84,6 +93,14 @@ class TrainEngine:
         # gradient bucket to the communication stream: reduce-scatter, AdamW
         # and all-gather of layer i overlap the backward of layers < i.
         overlap = self.fused_ddp is not None and not targets_may_be_ignored
+        if self.fused_ddp is not None:
+            # The fused step's bounded GPU barriers assume every rank reaches
+            # them within seconds of the others. A tiny NCCL all-reduce at the
+            # start of the step (which waits without a time limit, on the
+            # device, and never blocks the host) re-aligns the ranks after any
+            # host-side pause of one of them -- a checkpoint write, sampling,
+            # a slow data shard.
+            self.dist.align_streams()
         if overlap:
             self.opt.set_lr_mult(lr_mult)
         for i, (inputs, targets) in enumerate(batches):
@@ -129,6 +146,34 @@ class TrainEngine:
             L.sumsq(st.grad, out)
             return float(out.item()) ** 0.5
         return float(st.grad.double().pow(2).sum().item()) ** 0.5
+
+    def optimizer_state_dict(self) -> dict:
+        """AdamW state in the flat layout (``step_t``, full-length ``m`` and
+        ``v`` on the host). Collective under --backend fused (the moments are
+        sharded there): call it on every rank."""
+        if self.fused_ddp is not None:
+            return self.fused_ddp.gather_optimizer()
+        sd = self.opt.state_dict()
+        return {"step_t": sd["step_t"], "m": sd["m"].detach().cpu(), "v": sd["v"].detach().cpu()}
+
+    def load_optimizer_state_dict(self, sd: dict) -> None:
+        """Inverse of ``optimizer_state_dict`` (every rank passes the same state)."""
+        if self.fused_ddp is not None:
+            self.fused_ddp.load_optimizer(sd)
+        else:
+            self.opt.load_state_dict(sd)
+
+    def check_kernels(self, where: str) -> None:
+        """Raise if any of this package's kernels recorded an error (a bounded
+        wait that ran out, a rejected launch) since the last check. Every
+        device wait in the kernels gives up after a time limit instead of
+        hanging; this is where the host learns of it."""
+        if self.status_fn is None:
+            return
+        status = self.status_fn()
+        if status != 0:
+            raise KernelStatusError(f"device kernels reported error word {status:#x} ({where}); "
+                                    "results since the last check are not trustworthy")
 
     def sync_master(self) -> None:
         """Make the fp32 master weights complete on every rank (they are sharded

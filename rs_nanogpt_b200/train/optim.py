@@ -54,7 +54,9 @@ def mup_lr_scale(n_embd: int) -> float:
 
 class GroupedAdamW:
     def __init__(self, store: ParamStore, lrs: GroupLrs, n_embd: int, wd: GroupWeightDecay = GroupWeightDecay(),
-                 shard: Optional[Tuple[int, int]] = None):
+                 allocate_state: bool = True):
+        """``allocate_state=False`` leaves ``m``/``v`` unallocated: the fused
+        data-parallel step keeps only this rank's shard of them."""
         self.store = store
         s = mup_lr_scale(n_embd)
         self.base_lrs = GroupLrs(lrs.embedding * s, lrs.unembedding * s, lrs.matrix * s)
@@ -72,8 +74,11 @@ class GroupedAdamW:
         # The matrix group spans the block region; padding between tensors
         # stays zero (zero grad -> zero update on zero params).
         dev = store.device
-        self.m = torch.zeros(store.total, dtype=torch.float32, device=dev)
-        self.v = torch.zeros(store.total, dtype=torch.float32, device=dev)
+        self.m: Optional[torch.Tensor] = None
+        self.v: Optional[torch.Tensor] = None
+        if allocate_state:
+            self.m = torch.zeros(store.total, dtype=torch.float32, device=dev)
+            self.v = torch.zeros(store.total, dtype=torch.float32, device=dev)
 
     def current_lrs(self) -> GroupLrs:
         b = self.base_lrs
@@ -83,6 +88,7 @@ class GroupedAdamW:
         self.lr_mult = m
 
     def step(self, grad_scale: float = 1.0) -> None:
+        assert self.m is not None, "optimizer state is sharded; the fused data-parallel step owns it"
         self.step_t += 1
         st = self.store
         lrs = self.current_lrs()
@@ -99,12 +105,26 @@ class GroupedAdamW:
                 _adamw_torch(p, g, m, v, lr, b1, b2, eps, wd, self.step_t, grad_scale)
 
     def state_dict(self) -> dict:
+        """Full-length moments in the flat parameter layout plus the step count
+        (the resume file's contents)."""
+        assert self.m is not None, "optimizer state is sharded; use TrainEngine.optimizer_state_dict()"
         return {"step_t": self.step_t, "m": self.m, "v": self.v}
 
     def load_state_dict(self, sd: dict) -> None:
+        check_state_dict(sd, self.store.total)
         self.step_t = int(sd["step_t"])
-        self.m.copy_(sd["m"])
-        self.v.copy_(sd["v"])
+        if self.m is not None:
+            self.m.copy_(sd["m"])
+            self.v.copy_(sd["v"])
+
+
+def check_state_dict(sd: dict, total: int) -> None:
+    for k in ("step_t", "m", "v"):
+        if k not in sd:
+            raise ValueError(f"optimizer state is missing `{k}`")
+    for k in ("m", "v"):
+        if tuple(sd[k].shape) != (total,):
+            raise ValueError(f"optimizer state `{k}` has shape {tuple(sd[k].shape)}; this model needs ({total},)")
 
 
 @torch.no_grad()

@@ -103,11 +103,14 @@ def sample_prefix(tok, prompt: str, chat: bool) -> List[int]:
     return ids
 
 
-def train(engine: TrainEngine, batches, cfg: TrainConfig, ev: EvalContext, fault=None) -> float:
+def train(engine: TrainEngine, batches, cfg: TrainConfig, ev: EvalContext, fault=None, start_step: int = 0,
+          best_bpb: float = math.inf) -> float:
     """Runs the loop; returns the best val bpb seen (inf when eval is off).
     `batches.next_batch()` yields objects with `.inputs` / `.targets`.
     `fault`, when given, is called as fault(step, micro) before each
-    micro-batch (host-side fault injection for tests)."""
+    micro-batch (host-side fault injection for tests). A resumed run passes
+    the checkpoint's step as `start_step` (its weights and optimizer state are
+    those after `start_step` optimizer steps) and its val bpb as `best_bpb`."""
     from ..eval.sample import SampleOptions, cached_model, generate_ids
 
     from ..utils.mem import MemProbe
@@ -116,7 +119,7 @@ def train(engine: TrainEngine, batches, cfg: TrainConfig, ev: EvalContext, fault
     store = engine.store
     dist.broadcast_params(store.master)
     store.refresh_work()
-    best = math.inf
+    best = best_bpb
     t_start = time.perf_counter()
     probe = MemProbe.from_env(store.device) if dist.is_master() else None
     if probe is not None:
@@ -124,10 +127,12 @@ def train(engine: TrainEngine, batches, cfg: TrainConfig, ev: EvalContext, fault
         print(f"mem init         | {s0.summary()}", flush=True)
         ev.metrics.log(0, "mem", time.perf_counter() - t_start, **s0.record_fields())
         probe.reset_highs()
-    win_t, win_step = time.perf_counter(), 0
-    for step in range(cfg.num_iters + 1):
+    win_t, win_step = time.perf_counter(), start_step
+    for step in range(start_step, cfg.num_iters + 1):
         last = step == cfg.num_iters
-        if cadence_fires(step, cfg.num_iters, ev.eval_every):
+        resumed_here = step == start_step and start_step > 0
+        if cadence_fires(step, cfg.num_iters, ev.eval_every) and not resumed_here:
+            engine.check_kernels(f"before eval at step {step}")
             local = evaluate_shard_sums(engine, ev.val_batches, ev.token_bytes, dist.rank(), dist.world_size())
             m = BpbAccumulator.metrics_from_sums(dist.all_reduce_sums(local))
             if dist.is_master():
@@ -136,13 +141,18 @@ def train(engine: TrainEngine, batches, cfg: TrainConfig, ev: EvalContext, fault
             if m.bpb < best:
                 best = m.bpb
                 engine.sync_master()
+                opt_state = engine.optimizer_state_dict() if ev.save_optimizer else None  # collective
                 if dist.is_master():
                     checkpoint.save(f"{ev.ckpt_root}/best", store,
-                                    checkpoint.CheckpointMeta(store.cfg, step, m.bpb),
-                                    engine.opt if ev.save_optimizer else None)
-        if cadence_fires(step, cfg.num_iters, ev.sample_every):
+                                    checkpoint.CheckpointMeta(store.cfg, step, m.bpb), opt_state)
+                del opt_state
+                # Only the master wrote; the others wait here so no rank runs
+                # ahead into the next step's collectives while it is busy.
+                dist.barrier()
+        sampling = cadence_fires(step, cfg.num_iters, ev.sample_every) and not resumed_here
+        if sampling:
             engine.sync_master()
-        if dist.is_master() and cadence_fires(step, cfg.num_iters, ev.sample_every):
+        if dist.is_master() and sampling:
             opts = SampleOptions(ev.sample_tokens, ev.sample_temperature, 0, step)
             stops = ev.tokenizer.assistant_stop_ids() if ev.sample_chat else []
             prompts = CHAT_SAMPLE_PROMPTS if ev.sample_chat else SAMPLE_PROMPTS
@@ -150,6 +160,8 @@ def train(engine: TrainEngine, batches, cfg: TrainConfig, ev: EvalContext, fault
             for p in prompts:
                 ids = generate_ids(model, sample_prefix(ev.tokenizer, p, ev.sample_chat), opts, stops)
                 print(f"sample {p!r} -> {ev.tokenizer.decode_lossy(ids)!r}", flush=True)
+        if sampling:
+            dist.barrier()
         if last:
             break
         logging = step % cfg.log_every == 0
@@ -169,6 +181,7 @@ def train(engine: TrainEngine, batches, cfg: TrainConfig, ev: EvalContext, fault
         if nvtx:
             torch.cuda.nvtx.range_pop()
         if logging:
+            engine.check_kernels(f"step {step}")
             s, c = dist.all_reduce_sums([float(stats.nll_sum.item()), float(stats.valid_count.item())])
             mean_ce = float(np.float32(s) / np.float32(c)) if c > 0 else math.nan
             check_finite(mean_ce, step)

@@ -112,8 +112,11 @@ def save(directory: str, store, meta: CheckpointMeta, optimizer=None) -> None:
     with open(os.path.join(directory, META_FILE), "w") as f:
         f.write(write_meta(meta))
     if optimizer is not None:
-        torch.save({k: (v.cpu() if torch.is_tensor(v) else v) for k, v in optimizer.state_dict().items()},
-                   os.path.join(directory, OPTIM_FILE))
+        # `optimizer`: the flat state dict of TrainEngine.optimizer_state_dict().
+        sd = optimizer.state_dict() if hasattr(optimizer, "state_dict") else optimizer
+        tmp = os.path.join(directory, OPTIM_FILE + ".tmp")
+        torch.save({k: (v.cpu() if torch.is_tensor(v) else v) for k, v in sd.items()}, tmp)
+        os.replace(tmp, os.path.join(directory, OPTIM_FILE))
 
 
 def load_meta(directory: str) -> CheckpointMeta:
@@ -129,12 +132,18 @@ def load_meta(directory: str) -> CheckpointMeta:
 
 
 def load(directory: str, device) -> Tuple["ParamStore", CheckpointMeta]:
-    from safetensors.torch import load_file
-
     from ..models.params import ParamStore
 
     meta = load_meta(directory)
     store = ParamStore(meta.config, device)
+    load_weights_into(directory, store)
+    return store, meta
+
+
+def load_weights_into(directory: str, store) -> None:
+    """Copy a checkpoint's weights into an existing store of the same shapes."""
+    from safetensors.torch import load_file
+
     tensors = load_file(os.path.join(directory, MODEL_FILE))
     for name in store.names():
         if name not in tensors:
@@ -144,4 +153,23 @@ def load(directory: str, device) -> Tuple["ParamStore", CheckpointMeta]:
             raise CheckpointError(f"shape mismatch for {name}: {tuple(t.shape)} vs {store.slots[name].shape}")
         store.param(name).copy_(t.to(torch.float32))
     store.refresh_work()
-    return store, meta
+
+
+def load_optimizer(directory: str) -> dict:
+    """The ``optim.pt`` written by ``save(..., optimizer=...)``."""
+    path = os.path.join(directory, OPTIM_FILE)
+    if not os.path.exists(path):
+        raise CheckpointError(f"{path} does not exist; resuming needs a checkpoint saved with --save-optimizer")
+    return torch.load(path, map_location="cpu", weights_only=True)
+
+
+def resume(directory: str, engine) -> CheckpointMeta:
+    """Load a checkpoint's weights and optimizer state into a training engine
+    of the same architecture; returns its meta (``step`` = optimizer steps
+    taken). Every rank calls it with the same directory."""
+    meta = load_meta(directory)
+    if meta.config != engine.cfg:
+        raise CheckpointError(f"checkpoint config {meta.config} does not match the model being trained {engine.cfg}")
+    load_weights_into(directory, engine.store)
+    engine.load_optimizer_state_dict(load_optimizer(directory))
+    return meta

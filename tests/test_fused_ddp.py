@@ -1,6 +1,10 @@
 """Fused reduce-scatter + AdamW + all-gather kernel vs the NCCL all-reduce
-baseline on 2 GPUs: identical data, identical init, the parameters must agree
-after several optimizer steps. Needs at least 2 GPUs (skipped otherwise)."""
+baseline on 2, 4 and 8 GPUs (as many as the machine has): identical data,
+identical init and optimizer state, the parameters must agree after a step.
+Also checks the sharded optimizer state round trip (gather for a checkpoint,
+reshard on resume) and that a host-side pause of one rank longer than the
+kernels' 2 s barrier limit between steps does not desynchronize the ranks.
+Needs at least 2 GPUs (skipped otherwise)."""
 import os
 import subprocess
 import sys
@@ -13,7 +17,7 @@ pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 SCRIPT = r"""
-import os, sys, torch
+import os, sys, time, torch
 from rs_nanogpt_b200.config import GptConfig
 from rs_nanogpt_b200.models.params import ParamStore, init_params
 from rs_nanogpt_b200.ops._ext import kernel_status
@@ -50,9 +54,9 @@ for ignored in (False, True):
     norms = {}
     for backend, eng in engines.items():
         gm = torch.Generator(device=dev).manual_seed(77)
-        eng.opt.m.copy_(torch.randn(eng.opt.m.shape, device=dev, generator=gm) * 1e-3)
-        eng.opt.v.copy_(torch.rand(eng.opt.v.shape, device=dev, generator=gm) * 1e-5)
-        eng.opt.step_t = 4
+        total = eng.store.total
+        eng.load_optimizer_state_dict({"step_t": 4, "m": torch.randn(total, device=dev, generator=gm) * 1e-3,
+                                       "v": torch.rand(total, device=dev, generator=gm) * 1e-5})
         eng.step(batches[:2], 512, 0.7, targets_may_be_ignored=ignored)
         norms[backend] = eng.grad_norm()
         eng.sync_master()
@@ -66,15 +70,48 @@ for ignored in (False, True):
     assert diff < 1e-5, diff
     assert wdiff < 1e-2, wdiff
     assert abs(norms["nccl"] - norms["fused"]) < 1e-3 * max(1.0, norms["nccl"])
+    # Sharded moments gathered for a checkpoint equal the unsharded ones.
+    sa, sb = engines["nccl"].optimizer_state_dict(), engines["fused"].optimizer_state_dict()
+    assert sa["step_t"] == sb["step_t"] == 5
+    mdiff = (sa["m"] - sb["m"]).abs().max().item()
+    vdiff = (sa["v"] - sb["v"]).abs().max().item()
+    assert mdiff < 1e-6 and vdiff < 1e-8, (mdiff, vdiff)
+
+# Resume: reshard the gathered state into a fresh fused engine; its next step
+# equals the next step of the engine that kept running. Rank 0 pauses on the
+# host for 3 s before that step (longer than the 2 s device barrier limit).
+keep = engines["fused"]
+state = keep.optimizer_state_dict()
+keep.sync_master()
+fresh = make("fused")
+fresh.store.master.copy_(keep.store.master)
+fresh.store.refresh_work()
+fresh.load_optimizer_state_dict(state)
+for eng in (keep, fresh):
+    if dist.rank() == 0:
+        time.sleep(3.0)
+    eng.step(batches[1:], 512, 0.5)
+    eng.sync_master()
+torch.cuda.synchronize()
+rdiff = (keep.store.master - fresh.store.master).abs().max().item()
+print(f"rank {dist.rank()} resume diff {rdiff:.3e}", flush=True)
+assert kernel_status() == 0, "a device barrier timed out"
+assert rdiff < 1e-5, rdiff
 dist.shutdown()
 os._exit(0)
 """
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_fused_ddp_matches_nccl_baseline(tmp_path):
+def _gpus():
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fused_ddp_matches_nccl_baseline(tmp_path, world):
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
     from rs_nanogpt_b200.parallel.launcher import spawn_ranks, supervise_ranks
     script = tmp_path / "ddp.py"
     script.write_text(SCRIPT)
     env = {"PYTHONPATH": ROOT + os.pathsep + os.environ.get("PYTHONPATH", "")}
-    assert supervise_ranks(spawn_ranks(2, [sys.executable, str(script)], env)) == 0
+    assert supervise_ranks(spawn_ranks(world, [sys.executable, str(script)], env)) == 0

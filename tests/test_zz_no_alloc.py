@@ -70,3 +70,6 @@ def test_noalloc_rejects_oversized_problem():
     rc = fn(x.data_ptr(), x.data_ptr(), x.data_ptr(), lse.data_ptr(), x.data_ptr(), 64, 4096, 8, 128, stream)
     assert rc == 1
     assert b"exceeds" in err(rc)
+    # Within the scratch limit but more (batch, head) pairs than grid.y holds.
+    rc = fn(x.data_ptr(), x.data_ptr(), x.data_ptr(), lse.data_ptr(), x.data_ptr(), 65536, 1, 1, 128, stream)
+    assert rc == 2 and b"65535" in err(rc)
