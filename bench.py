@@ -50,10 +50,87 @@ def parse():
     return p.parse_args()
 
 
+REF_SRC = os.path.join(ROOT, "baseline", "_ref")
+REF_ORIG = "/root/reference"
+
+
+def _probe_reference():
+    """What is on this machine for building the reference (a Rust/candle
+    program built with `cargo build --release --features nccl`): returns
+    (cargo path or None, reference source dir or None, candle source or None,
+    list of findings)."""
+    import glob
+    import shutil
+    found = []
+    cargo = shutil.which("cargo")
+    found.append(f"cargo: {cargo or 'not on PATH'}")
+    rustc = shutil.which("rustc")
+    found.append(f"rustc: {rustc or 'not on PATH'}")
+    src = None
+    for cand in (REF_SRC, REF_ORIG):
+        if os.path.exists(os.path.join(cand, "Cargo.toml")):
+            src = cand
+            break
+    installed = os.path.isdir(REF_SRC) and os.listdir(REF_SRC)
+    found.append(f"baseline/_ref: {'present' if installed else 'absent (pip cannot install a Cargo project)'}")
+    found.append(f"reference source: {src or 'not found'}")
+    candle = None
+    roots = [os.path.expanduser("~/.cargo/registry"), os.path.expanduser("~/.cargo/git/checkouts")]
+    if src:
+        roots += [os.path.join(src, "vendor")]
+    for r in roots:
+        hits = glob.glob(os.path.join(r, "**", "candle-core*"), recursive=True)
+        if hits:
+            candle = hits[0]
+            break
+    found.append(f"vendored candle: {candle or 'none (candle is a git dependency, no network to fetch it)'}")
+    return cargo, src, candle, found
+
+
 def reference_arm(args):
-    reason = ("the reference is a Rust/candle program; no Rust toolchain (cargo) exists in this image and its "
-              "candle git dependency cannot be fetched offline, so it cannot be built or run")
-    print(json.dumps({"impl": "reference", "unavailable": reason}))
+    """Runs the reference through its own CLI when it can be built here
+    offline; otherwise prints what the probe found."""
+    import shutil
+    import subprocess
+    import tempfile
+    cargo, src, candle, found = _probe_reference()
+    if not (cargo and src and candle):
+        print(json.dumps({"impl": "reference", "unavailable": "cannot build the reference offline: " +
+                          "; ".join(found)}))
+        return
+    work = tempfile.mkdtemp(prefix="ref_build_")
+    tree = os.path.join(work, "src")
+    shutil.copytree(src, tree)
+    r = subprocess.run([cargo, "build", "--release", "--offline", "--features", "nccl" if args.gpus > 1 else "cuda"],
+                       cwd=tree, capture_output=True, text=True)
+    if r.returncode != 0:
+        print(json.dumps({"impl": "reference", "unavailable": "offline cargo build failed: " +
+                          r.stderr.strip().splitlines()[-1][:300] if r.stderr.strip() else "no output"}))
+        return
+    binary = os.path.join(tree, "target", "release", "rs-nanogpt")
+    from rs_nanogpt_b200 import _host
+    from rs_nanogpt_b200.data.synthetic import write_corpus
+    data = os.path.join(work, "data")
+    write_corpus(data, shards=4, docs_per_shard=4000, seed=0)
+    vocab = os.path.join(work, "vocab.txt")
+    _host.write_vocab(vocab, [])
+    cmd = [binary, "pretrain", "--data", data, "--vocab", vocab, "--gpus", str(args.gpus),
+           "--n-layer", str(args.depth), "--n-embd", str(64 * args.depth), "--n-head", str(args.depth // 2),
+           "--sequence-len", str(args.seq), "--device-batch", str(args.device_batch),
+           "--total-batch", str(args.total_batch), "--num-iters", str(args.warmup + args.steps),
+           "--log-every", "1", "--eval-every", "0", "--out", os.path.join(work, "out")]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    rates = [float(l.split("tok/s")[0].split("|")[-1]) for l in r.stdout.splitlines() if "tok/s" in l]
+    timed = rates[args.warmup:]
+    if r.returncode != 0 or not timed:
+        print(json.dumps({"impl": "reference", "unavailable": f"reference run failed (rc {r.returncode})"}))
+        return
+    value = sum(timed) / len(timed)
+    print(json.dumps({"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+                      "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": args.total_batch / value * 1e3, "higher_is_better": True,
+                      "timing": "the reference's own per-step log (wall clock)", "dtype": "bf16",
+                      "data": "synthetic corpus, byte-level vocab (vocab 256 + specials)"}))
 
 
 def measured_peak_tflops():
@@ -93,6 +170,11 @@ def main():
     accum = args.total_batch // per
     tokens_per_rank = args.total_batch // n
 
+    ddp_check = None
+    if n > 1 and args.backend == "fused":
+        from rs_nanogpt_b200.parallel.check import fused_vs_nccl
+        ddp_check = fused_vs_nccl(dist, device)
+
     store = ParamStore(cfg, device)
     init_params(store, seed=1234, mode="bench")
     dist.broadcast_params(store.master)
@@ -120,9 +202,14 @@ def main():
     for _ in range(args.warmup):
         engine.step(dev_batches, tokens_per_rank, 1.0)
     l0 = launch_count()
+    engine.tail_events = [] if engine.fused_ddp is not None else None
     with ClockSampler() as clocks:
         ms = timed_device(args.steps)
     launches = launch_count() - l0
+    tail_ms = None
+    if engine.tail_events:
+        tail_ms = dist.max_over_ranks(sum(a.elapsed_time(b) for a, b in engine.tail_events) / len(engine.tail_events))
+    engine.tail_events = None
     ms = dist.max_over_ranks(ms)
     status = kernel_status()
 
@@ -171,6 +258,12 @@ def main():
             "gpu_launches_note": "kernels of this package launched in the timed region (per rank)",
             "kernel_status": status, "e2e": e2e,
         }
+        if ddp_check is not None:
+            out["ddp_check"] = ddp_check
+        if tail_ms is not None:
+            out["exposed_comm_tail_ms"] = tail_ms
+            out["exposed_comm_tail_note"] = ("device time from the end of the last micro-batch's backward to the end "
+                                             "of the fused step's closing barrier, mean per step, max over ranks")
         print(json.dumps(out))
     dist.shutdown()
 

@@ -2,29 +2,37 @@
 // (tcgen05 + TMEM + TMA), head_dim 128, seq_len a multiple of 128.
 //
 // One CTA = one block of 128 keys of one (batch, head). K and V stay in
-// shared memory; for every query block j >= the key block (causal) it
-//   MMA1  S^T  = K  Q_j^T            -> TMEM [0,128)
-//   MMA2  dP^T = V  dO_j^T           -> TMEM [128,256)
-//   (compute warps, thread = key row)
-//         P^T  = exp2(S^T * scale*log2e - lse2[q])   (causal mask on the diagonal)
+// shared memory; the CTA walks the query blocks of 64 rows j that can see its
+// keys (causal) and for each one
+//   S^T  = K  Q_j^T                     (M 128 keys, N 64 queries)
+//   dP^T = V  dO_j^T
+//   (softmax warps, thread = key row)
+//         P^T  = exp2(S^T * scale*log2e - lse2[q])   (causal mask near the diagonal)
 //         dS^T = P^T o (dP^T - D[q])
 //         P^T goes back to tensor memory (bf16 pairs, over the S^T columns just
 //         read); dS^T goes to shared memory.
-//   MMA3  dV  += P^T  dO_j           -> TMEM [384,512) (A operand from TMEM)
-//   MMA4  dK  += dS^T Q_j            -> TMEM [256,384)
-//   MMA5  dQ_j = dS K                -> TMEM [128,256) (dS^T's smem tile read as
-//                                       an MN-major A operand: no transpose copy)
-//   (drain warps, thread = query row) dQ_j * scale is added to an fp32
-//   accumulator with TMA reduce-add tensor stores, staged through dS^T's
-//   shared-memory tile once MMA5 has consumed it.
-// Q_j / dO_j (and their LSE / D rows) are double-buffered.
-// After the last block the compute warps write dK * scale (with the RoPE /
+//   dQ_j^T = K^T dS^T                   (M 128 = head_dim, N 64 queries), into
+//                                        the dP^T columns the softmax just read
+//   dV  += P^T  dO_j                    (A operand from tensor memory)
+//   dK  += dS^T Q_j
+//   (drain warps, thread = head-dim lane) dQ_j * scale is added to an fp32
+//   accumulator with TMA reduce-add tensor stores.
+//
+// Tensor memory (512 columns): S^T [0,64) and [64,128) and dP^T / dQ^T
+// [128,192) and [192,256) for two query blocks in flight, dK [256,384),
+// dV [384,512). With two score buffers the MMA warp issues block j+1's S^T and
+// dP^T before block j's gradient products, so the softmax-gradient math of
+// block j overlaps five MMAs (those of block j-1 and the scores of j+1) and
+// the drain of dQ_{j-1} overlaps three (dV_{j-1}, dK_{j-1}, S_{j+1}); the
+// issue order per block is dQ, dV, dK so the drain starts as early as
+// possible. Q_j / dO_j (and their LSE / D rows) rotate through three stages.
+// After the last block the softmax warps write dK * scale (with the RoPE /
 // QK-norm backward when requested) and dV (bf16) into the gradient buffer. A
 // final small kernel converts the dQ accumulator to bf16.
 //
-// Warps: 0 = TMA/bulk loads, 1 = TMEM allocation + MMA issue, 2-9 = compute
-// (two per TMEM lane quarter), 10-13 = dQ drain. Every wait is bounded
-// (common.cuh).
+// Warps: 0 = TMA/bulk loads, 1 = TMEM allocation + MMA issue, 2-9 = softmax
+// gradient (two per TMEM lane quarter, 32 query columns each), 10-13 = dQ
+// drain. Every wait is bounded (common.cuh).
 #include <cstdlib>
 
 #include <ATen/cuda/CUDAContext.h>
@@ -38,15 +46,21 @@
 namespace nk {
 
 namespace fb {
-constexpr int HD = 128, BK = 128, BQ = 128;
-constexpr int kThreads = 448;  // 2 + 8 compute + 4 drain warps
-constexpr int kTile = 128 * 128 * 2;   // 32 KB
-constexpr int kSub = 128 * 64 * 2;     // 16 KB swizzle sub-tile
-constexpr int kStage = 32 * 32 * 4;  // 4 KB: one drain warp's 32 x 32 fp32 dQ chunk
-// K, V, Q x2, dO x2, dS^T (also the dQ drain staging) + LSE/D x2 + barriers.
+constexpr int HD = 128, BK = 128, BQ = 64, NS = 3;
+constexpr int kThreads = 448;            // 2 + 8 softmax + 4 drain warps
+constexpr int kKTile = 128 * 128 * 2;    // 32 KB: K or V (two 64-column sub-tiles)
+constexpr int kKSub = 128 * 64 * 2;      // 16 KB
+constexpr int kQTile = BQ * 128 * 2;     // 16 KB: one query block of Q or dO
+constexpr int kQSub = BQ * 64 * 2;       // 8 KB
+constexpr int kDsTile = 128 * BQ * 2;    // 16 KB: dS^T [key][query], one 128-byte-row sub-tile
+constexpr int kStage = 32 * 32 * 4;      // 4 KB: one drain warp's 32 x 32 fp32 dQ chunk
+constexpr int kOffK = 0, kOffV = kKTile, kOffQ = 2 * kKTile, kOffO = kOffQ + NS * kQTile,
+              kOffDs = kOffO + NS * kQTile, kOffStage = kOffDs + 2 * kDsTile,
+              kOffLD = kOffStage + 4 * 2 * kStage, kOffBar = kOffLD + NS * 2 * BQ * 4;
 // No alignment slack: the dynamic shared memory base is checked to be
 // 1024-byte aligned at run time (the kernel reports an error otherwise).
-constexpr int kSmem = 7 * kTile + 2 * 2 * BQ * 4 + 256;
+constexpr int kSmem = kOffBar + 256;
+static_assert(kSmem <= 232448, "shared memory budget");
 }  // namespace fb
 
 struct FbArgs {
@@ -69,10 +83,6 @@ struct FbArgs {
   int dbg;
 };
 
-__device__ __forceinline__ uint32_t tile_off(int r, int c) {  // 16B chunk c (of 16) in row r, K-major SW128
-  return uint32_t((c >> 3) * fb::kSub + r * 128 + (((c & 7) ^ (r & 7)) << 4));
-}
-
 __global__ void __launch_bounds__(fb::kThreads, 1)
     flash_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tmo,
                         const __grid_constant__ CUtensorMap tmq, const FbArgs a) {
@@ -83,44 +93,45 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
     if (threadIdx.x == 0) atomicCAS(a.err, 0, kErrTimeoutOther);
     return;
   }
-  uint8_t* sK = smem;
-  uint8_t* sV = smem + kTile;
-  uint8_t* sQ = smem + 2 * kTile;   // [2] query blocks
-  uint8_t* sO = smem + 4 * kTile;   // [2] dO blocks
-  uint8_t* sS = smem + 6 * kTile;   // dS^T [key][query]; after the dQ product, the drain staging
-  float* sL = reinterpret_cast<float*>(smem + 7 * kTile);  // [2] lse2 of the query block
-  float* sD = sL + 2 * BQ;                                 // [2] D of the query block
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 7 * kTile + 4 * BQ * 4);
+  uint8_t* sK = smem + kOffK;
+  uint8_t* sV = smem + kOffV;
+  uint8_t* sQ = smem + kOffQ;    // [NS] query blocks
+  uint8_t* sO = smem + kOffO;    // [NS] dO blocks
+  uint8_t* sDs = smem + kOffDs;  // [2] dS^T tiles
+  float* sL = reinterpret_cast<float*>(smem + kOffLD);  // [NS] lse2 of the query block
+  float* sD = sL + NS * BQ;                             // [NS] D of the query block
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qd_full = bars + 1;   // [2]
-  uint64_t* qd_empty = bars + 3;  // [2]
-  uint64_t* st_full = bars + 5;
-  uint64_t* p_full = bars + 6;
-  uint64_t* dq_full = bars + 7;
-  uint64_t* dq_free = bars + 8;
-  uint64_t* kv_done = bars + 9;
-  uint64_t* stage_free = bars + 10;  // the drain's staging reads of dS^T's tile are done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  uint64_t* qd_full = bars + 1;    // [NS]
+  uint64_t* qd_empty = bars + 4;   // [NS]
+  uint64_t* st_full = bars + 7;    // [2] S^T and dP^T of a block are in tensor memory
+  uint64_t* p_full = bars + 9;     // [2] P^T (tensor memory) and dS^T (shared memory) written
+  uint64_t* dq_full = bars + 11;   // [2] dQ^T of a block is in tensor memory
+  uint64_t* dq_free = bars + 13;   // [2] ... and has been read out by the drain warps
+  uint64_t* kv_done = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int kb = blockIdx.x;  // key block; low blocks have the most query blocks
   const int b = blockIdx.y / a.H, h = blockIdx.y % a.H;
   const int nq = a.T / BQ;
-  const int nblk = nq - kb;   // query blocks kb .. nq-1
+  const int j0 = kb * (BK / BQ);  // first query block that sees a key of this block
+  const int nblk = nq - j0;
   const long bh = long(b) * a.H + h;
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NS; ++i) {
       mbar_init(&qd_full[i], 1);
       mbar_init(&qd_empty[i], 1);
     }
-    mbar_init(st_full, 1);
-    mbar_init(p_full, 8);
-    mbar_init(dq_full, 1);
-    mbar_init(dq_free, 4);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&st_full[i], 1);
+      mbar_init(&p_full[i], 8);
+      mbar_init(&dq_full[i], 1);
+      mbar_init(&dq_free[i], 4);
+    }
     mbar_init(kv_done, 1);
-    mbar_init(stage_free, 4);
     fence_barrier_init();
     prefetch_tmap(&tm);
     prefetch_tmap(&tmo);
@@ -129,106 +140,118 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;  // S^T @0, dP^T / dQ @128, dK @256, dV @384
+  const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
     if (lane == 0) {
       const int xq = h * HD, xk = a.C + h * HD, xv = 2 * a.C + h * HD;
-      mbar_arrive_expect_tx(kv_full, 2 * kTile);
-      for (int s = 0; s < 2; ++s) {
-        tma_load_3d(sK + s * kSub, &tm, kv_full, xk + 64 * s, kb * BK, b);
-        tma_load_3d(sV + s * kSub, &tm, kv_full, xv + 64 * s, kb * BK, b);
-      }
-      for (int n = 0; n < nblk; ++n) {
-        const int j = kb + n, u = n & 1;
-        if (!mbar_wait(&qd_empty[u], ((n >> 1) & 1) ^ 1, kErrTimeoutProducer, a.err)) break;
-        mbar_arrive_expect_tx(&qd_full[u], 2 * kTile + 2 * BQ * 4);
-        for (int s = 0; s < 2; ++s) {
-          tma_load_3d(sQ + u * kTile + s * kSub, &tm, &qd_full[u], xq + 64 * s, j * BQ, b);
-          tma_load_3d(sO + u * kTile + s * kSub, &tmo, &qd_full[u], h * HD + 64 * s, j * BQ, b);
+      mbar_arrive_expect_tx(kv_full, 2 * kKTile);
+      for (int s = 0; s < 2; ++s)
+        for (int r = 0; r < 2; ++r) {  // 64-row boxes: the second lands 8 KB into the sub-tile
+          tma_load_3d(sK + s * kKSub + r * kQSub, &tm, kv_full, xk + 64 * s, kb * BK + 64 * r, b);
+          tma_load_3d(sV + s * kKSub + r * kQSub, &tm, kv_full, xv + 64 * s, kb * BK + 64 * r, b);
         }
-        bulk_load(sL + u * BQ, a.lse + bh * a.T + j * BQ, BQ * 4, &qd_full[u]);
-        bulk_load(sD + u * BQ, a.dsum + bh * a.T + j * BQ, BQ * 4, &qd_full[u]);
+      for (int n = 0; n < nblk; ++n) {
+        const int j = j0 + n, st = n % NS;
+        if (!mbar_wait(&qd_empty[st], ((n / NS) & 1) ^ 1, kErrTimeoutProducer, a.err)) break;
+        mbar_arrive_expect_tx(&qd_full[st], 2 * kQTile + 2 * BQ * 4);
+        for (int s = 0; s < 2; ++s) {
+          tma_load_3d(sQ + st * kQTile + s * kQSub, &tm, &qd_full[st], xq + 64 * s, j * BQ, b);
+          tma_load_3d(sO + st * kQTile + s * kQSub, &tmo, &qd_full[st], h * HD + 64 * s, j * BQ, b);
+        }
+        bulk_load(sL + st * BQ, a.lse + bh * a.T + j * BQ, BQ * 4, &qd_full[st]);
+        bulk_load(sD + st * BQ, a.dsum + bh * a.T + j * BQ, BQ * 4, &qd_full[st]);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t id_kk = idesc_bf16(128, 128, false, false);  // MMA1, MMA2
-      const uint32_t id_kn = idesc_bf16(128, HD, false, true);    // MMA3, MMA4: B MN-major
-      const uint32_t id_nn = idesc_bf16(128, HD, true, true);     // MMA5: A and B MN-major
-      const uint32_t k = smem_u32(sK), v = smem_u32(sV), ds = smem_u32(sS);
-      bool ok = mbar_wait(kv_full, 0, kErrTimeoutMma, a.err);
+      const uint32_t id_s = idesc_bf16(128, BQ, false, false);  // S^T, dP^T
+      const uint32_t id_kn = idesc_bf16(128, HD, false, true);  // dV, dK: B MN-major
+      const uint32_t id_q = idesc_bf16(128, BQ, true, true);    // dQ^T: A and B MN-major
+      const uint32_t k = smem_u32(sK), v = smem_u32(sV);
+      // Scores of block n into buffer n & 1.
+      auto scores = [&](int n) -> bool {
+        const int st = n % NS, u = n & 1;
+        if (!mbar_wait(&qd_full[st], (n / NS) & 1, kErrTimeoutMma, a.err)) return false;
+        tc_fence_after();
+        const uint32_t q = smem_u32(sQ + st * kQTile), o = smem_u32(sO + st * kQTile);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t ka = (kk >> 2) * kKSub + (kk & 3) * 32, qa = (kk >> 2) * kQSub + (kk & 3) * 32;
+          umma_bf16(tmem + 64 * u, sw128_desc(k + ka, 16, 1024), sw128_desc(q + qa, 16, 1024), id_s, kk > 0);
+        }
+        // dP^T reuses the columns of dQ^T of block n - 2: wait until it was drained.
+        if (n >= 2 && !mbar_wait(&dq_free[u], ((n - 2) >> 1) & 1, kErrTimeoutMma, a.err)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t ka = (kk >> 2) * kKSub + (kk & 3) * 32, qa = (kk >> 2) * kQSub + (kk & 3) * 32;
+          umma_bf16(tmem + 128 + 64 * u, sw128_desc(v + ka, 16, 1024), sw128_desc(o + qa, 16, 1024), id_s,
+                    kk > 0);
+        }
+        umma_commit(&st_full[u]);
+        return true;
+      };
+      bool ok = mbar_wait(kv_full, 0, kErrTimeoutMma, a.err) && scores(0);
       for (int n = 0; n < nblk && ok; ++n) {
-        const int u = n & 1;
-        const uint32_t q = smem_u32(sQ + u * kTile), o = smem_u32(sO + u * kTile);
-        if (!mbar_wait(&qd_full[u], (n >> 1) & 1, kErrTimeoutMma, a.err)) break;
+        const int st = n % NS, u = n & 1;
+        if (n + 1 < nblk && !scores(n + 1)) break;
+        if (!mbar_wait(&p_full[u], (n >> 1) & 1, kErrTimeoutMma, a.err)) break;
         tc_fence_after();
+        const uint32_t q = smem_u32(sQ + st * kQTile), o = smem_u32(sO + st * kQTile);
+        const uint32_t ds = smem_u32(sDs + u * kDsTile);
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kSub + (kk & 3) * 32;
-          umma_bf16(tmem + 0, sw128_desc(k + off, 16, 1024), sw128_desc(q + off, 16, 1024), id_kk, kk > 0);
-        }
-        // dP^T reuses the columns of the previous dQ (and the compute warps
-        // reuse dS^T's tile, the drain's staging): wait until it was drained.
-        if (n > 0 && !mbar_wait(dq_free, (n - 1) & 1, kErrTimeoutMma, a.err)) break;
-        tc_fence_after();
+        for (int kk = 0; kk < BK / 16; ++kk)  // dQ^T = K^T dS^T: contraction over the 128 keys
+          umma_bf16(tmem + 128 + 64 * u, sw128_desc(k + kk * 2048, kKSub, 1024),
+                    sw128_desc(ds + kk * 2048, kDsTile, 1024), id_q, kk > 0);
+        umma_commit(&dq_full[u]);
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kSub + (kk & 3) * 32;
-          umma_bf16(tmem + 128, sw128_desc(v + off, 16, 1024), sw128_desc(o + off, 16, 1024), id_kk, kk > 0);
-        }
-        umma_commit(st_full);
-        if (!mbar_wait(p_full, n & 1, kErrTimeoutMma, a.err)) break;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < BQ / 16; ++kk) {  // contraction over the 128 queries
+        for (int kk = 0; kk < BQ / 16; ++kk) {  // contraction over the 64 queries
           // P^T is in tensor memory: 32 query columns of chunk c packed as bf16
-          // pairs in TMEM columns [32c, 32c + 16) (written over S^T).
-          umma_bf16_ts(tmem + 384, tmem + 32 * (kk >> 1) + 8 * (kk & 1), sw128_desc(o + kk * 2048, kSub, 1024),
-                       id_kn, (n > 0 || kk > 0) ? 1u : 0u);
-          const uint32_t aoff = (kk >> 2) * kSub + (kk & 3) * 32;
-          umma_bf16(tmem + 256, sw128_desc(ds + aoff, 16, 1024), sw128_desc(q + kk * 2048, kSub, 1024), id_kn,
+          // pairs in TMEM columns [64u + 32c, 64u + 32c + 16) (written over S^T).
+          umma_bf16_ts(tmem + 384, tmem + 64 * u + 32 * (kk >> 1) + 8 * (kk & 1),
+                       sw128_desc(o + kk * 2048, kQSub, 1024), id_kn, (n > 0 || kk > 0) ? 1u : 0u);
+          umma_bf16(tmem + 256, sw128_desc(ds + kk * 32, 16, 1024), sw128_desc(q + kk * 2048, kQSub, 1024), id_kn,
                     (n > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&qd_empty[u]);  // Q_j / dO_j are no longer read
-#pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk) {  // contraction over the 128 keys
-          umma_bf16(tmem + 128, sw128_desc(ds + kk * 2048, kSub, 1024), sw128_desc(k + kk * 2048, kSub, 1024),
-                    id_nn, kk > 0);
-        }
-        umma_commit(dq_full);
+        umma_commit(&qd_empty[st]);  // Q_j / dO_j / their LSE and D rows are no longer read
       }
       umma_commit(kv_done);
     }
   } else if (warp < 10) {
-    // Compute warps: thread = key row; two warps per TMEM lane quarter, each
-    // taking 64 of the block's 128 query columns.
+    // Softmax-gradient warps: thread = key row; two warps per TMEM lane
+    // quarter, each taking 32 of the block's 64 query columns.
     const int quarter = warp & 3;
-    const int half = (warp - 2) / 4;
+    const int half = (warp - 2) / 4;  // query chunk of this warp
     const int r = quarter * 32 + lane;
     const int key = kb * BK + r;
     const uint32_t lanes = uint32_t(quarter * 32) << 16;
     bool ok = true;
-    // P^T (into tensor memory, over this chunk's own S^T columns) and dS^T
-    // (shared memory) for the 32 query columns starting at c * 32.
-    auto chunk = [&](int c, int j, bool diag, int u) {
+    for (int n = 0; n < nblk && ok; ++n) {
+      const int j = j0 + n, u = n & 1, st = n % NS;
+      // st_full of block n is committed after every MMA of block n - 2, so
+      // dS^T tile u (read by dK / dQ of block n - 2) is free as well.
+      if (!mbar_wait(&st_full[u], (n >> 1) & 1, kErrTimeoutEpilogue, a.err)) { ok = false; break; }
+      tc_fence_after();
       float s[32], dp[32];
-      tmem_ld_32x32(tmem + lanes + c * 32, s);
-      tmem_ld_32x32(tmem + lanes + 128 + c * 32, dp);
-      const float* L = sL + u * BQ;
-      const float* D = sD + u * BQ;
+      tmem_ld_32x32(tmem + lanes + 64 * u + 32 * half, s);
+      tmem_ld_32x32(tmem + lanes + 128 + 64 * u + 32 * half, dp);
+      const float* L = sL + st * BQ + 32 * half;
+      const float* D = sD + st * BQ + 32 * half;
+      const bool diag = n < BK / BQ;
+      const int q0 = j * BQ + 32 * half;
       uint32_t pp[16], dd[16];
 #pragma unroll
       for (int i = 0; i < 32; i += 4) {
-        const float4 l4 = *reinterpret_cast<const float4*>(L + c * 32 + i);
-        const float4 d4 = *reinterpret_cast<const float4*>(D + c * 32 + i);
+        const float4 l4 = *reinterpret_cast<const float4*>(L + i);
+        const float4 d4 = *reinterpret_cast<const float4*>(D + i);
         const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
         float pv[4], gv[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           if (a.dbg & 2) { pv[e] = s[i + e]; gv[e] = dp[i + e]; continue; }
           pv[e] = exp2f(fmaf(s[i + e], a.sl2, -lv[e]));
-          if (diag && (j * BQ + c * 32 + i + e) < key) pv[e] = 0.f;
+          if (diag && (q0 + i + e) < key) pv[e] = 0.f;
           gv[e] = pv[e] * (dp[i + e] - dv4[e]);
         }
         pp[i / 2] = pack_bf16x2(pv[0], pv[1]);
@@ -236,30 +259,18 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
         dd[i / 2] = pack_bf16x2(gv[0], gv[1]);
         dd[i / 2 + 1] = pack_bf16x2(gv[2], gv[3]);
       }
-      tmem_st_32x16(tmem + lanes + c * 32, pp);
+      tmem_st_32x16(tmem + lanes + 64 * u + 32 * half, pp);
+      uint8_t* ds = sDs + u * kDsTile;
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
-        *reinterpret_cast<uint4*>(sS + tile_off(r, c * 4 + q)) = make_uint4(dd[4 * q], dd[4 * q + 1], dd[4 * q + 2], dd[4 * q + 3]);
-    };
-    for (int n = 0; n < nblk && ok; ++n) {
-      const int j = kb + n, u = n & 1;
-      if (!mbar_wait(st_full, n & 1, kErrTimeoutEpilogue, a.err)) { ok = false; break; }
-      tc_fence_after();
-      // st_full of block n comes after the previous block's dQ product and
-      // TMEM drain (dP^T waited for it); dS^T's tile is also the drain's
-      // staging, so wait for its reads too.
-      if (n > 0 && !mbar_wait(stage_free, (n - 1) & 1, kErrTimeoutEpilogue, a.err)) { ok = false; break; }
-      if (n == 0) {  // the diagonal block: causal mask
-        chunk(2 * half, j, true, u);
-        chunk(2 * half + 1, j, true, u);
-      } else {
-        chunk(2 * half, j, false, u);
-        chunk(2 * half + 1, j, false, u);
+      for (int c = 0; c < 4; ++c) {  // 16-byte chunk 4 * half + c of row r, 128-byte swizzle
+        const int cc = 4 * half + c;
+        *reinterpret_cast<uint4*>(ds + r * 128 + ((cc ^ (r & 7)) << 4)) =
+            make_uint4(dd[4 * c], dd[4 * c + 1], dd[4 * c + 2], dd[4 * c + 3]);
       }
       fence_proxy_async();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&p_full[u]);
     }
     if (ok && mbar_wait(kv_done, 0, kErrTimeoutEpilogue, a.err)) {
       tc_fence_after();
@@ -366,46 +377,43 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       }
     }
   } else {
-    // dQ drain warps: thread = query row of the current block. Each warp
-    // stages 32 rows x 32 columns of dQ * scale (fp32, 128B-swizzled) and
-    // adds them to the fp32 accumulator with one TMA reduce-add; two staging
-    // buffers per warp let the next chunk fill while the previous one drains.
+    // dQ drain warps: thread = head-dim lane (TMEM lane) of dQ^T, 32 query
+    // columns per chunk. Each warp stages 32 queries x 32 head dims of
+    // dQ * scale (fp32, row-major 128-byte rows: lane t writes word t of every
+    // row, conflict-free) and adds them to the fp32 accumulator with one TMA
+    // reduce-add; two staging buffers per warp let the next chunk fill while
+    // the previous one drains.
     const int quarter = warp & 3;
     const uint32_t lanes = uint32_t(quarter * 32) << 16;
-    uint8_t* stage = sS + (warp - 10) * 2 * kStage;  // dS^T's tile: free once dQ = dS K is done
+    float* stage = reinterpret_cast<float*>(smem + kOffStage + (warp - 10) * 2 * kStage);
     int chunks = 0;
     for (int n = 0; n < nblk; ++n) {
-      const int j = kb + n;
-      if (!mbar_wait(dq_full, n & 1, kErrTimeoutEpilogue, a.err)) break;
+      const int j = j0 + n, u = n & 1;
+      if (!mbar_wait(&dq_full[u], (n >> 1) & 1, kErrTimeoutEpilogue, a.err)) break;
       tc_fence_after();
-#pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c, ++chunks) {
-        float x[32];
-        tmem_ld_32x32(tmem + lanes + 128 + c * 32, x);
-        if (a.dbg & 1) continue;
-        uint8_t* buf = stage + (chunks & 1) * kStage;
-        if (lane == 0 && c >= 2) bulk_wait_read<1>();  // this buffer's previous reduce has read it
+      float x[2][32];
+      tmem_ld_32x32(tmem + lanes + 128 + 64 * u, x[0]);
+      tmem_ld_32x32(tmem + lanes + 128 + 64 * u + 32, x[1]);
+      // The dQ^T columns are free for the scores of block n + 2.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&dq_free[u]);
+      if (a.dbg & 1) continue;
+#pragma unroll
+      for (int c = 0; c < 2; ++c, ++chunks) {
+        float* buf = stage + (chunks & 1) * (kStage / 4);
+        if (lane == 0 && chunks >= 2) bulk_wait_read<1>();  // this buffer's previous reduce has read it
         __syncwarp();
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          *reinterpret_cast<float4*>(buf + lane * 128 + ((k ^ (lane & 7)) << 4)) =
-              make_float4(x[4 * k] * a.scale, x[4 * k + 1] * a.scale, x[4 * k + 2] * a.scale, x[4 * k + 3] * a.scale);
+        for (int i = 0; i < 32; ++i) buf[i * 32 + lane] = x[c][i] * a.scale;
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) {
           asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];"
-                       ::"l"(&tmq), "r"(smem_u32(buf)), "r"(h * HD + c * 32), "r"(b * a.T + j * BQ + quarter * 32)
+                       ::"l"(&tmq), "r"(smem_u32(buf)), "r"(h * HD + quarter * 32), "r"(b * a.T + j * BQ + 32 * c)
                        : "memory");
           bulk_commit();
         }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_free);  // dQ's TMEM columns are free for the next dP^T
-      // The staging reads must be done before the compute warps rewrite dS^T.
-      if (lane == 0) {
-        bulk_wait_read<0>();
-        mbar_arrive(stage_free);
       }
     }
     if (lane == 0) bulk_wait<0>();
@@ -460,12 +468,13 @@ __global__ void dq_finish_kernel(const float* __restrict__ acc, __nv_bfloat16* _
 bool flash_bwd_tc_supported(int64_t T, int64_t HD) { return HD == 128 && T % 128 == 0; }
 
 // 3-D map over a (B*T, width) bf16 activation: inner `width` columns, then the
-// T rows of one sequence, then B sequences (rows past a sequence read as zeros).
+// T rows of one sequence, then B sequences (rows past a sequence read as zeros);
+// the box is 64 columns x 64 rows.
 static CUtensorMap seq_map_3d(void* base, int64_t B, int64_t T, int64_t width) {
   CUtensorMap m;
   cuuint64_t dims[3] = {cuuint64_t(width), cuuint64_t(T), cuuint64_t(B)};
   cuuint64_t strides[2] = {cuuint64_t(width * 2), cuuint64_t(T * width * 2)};
-  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t box[3] = {64, uint32_t(fb::BQ), 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = encode_tiled_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr,
                                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -525,7 +534,7 @@ void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torc
     cuuint32_t estr[2] = {1, 1};
     TORCH_CHECK(reinterpret_cast<uintptr_t>(dq_acc.data_ptr()) % 16 == 0, "flash_bwd_tc: dq_acc alignment");
     CUresult r = encode_tiled_fn()(&tmq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dq_acc.data_ptr(), dims, strides, box,
-                                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     TORCH_CHECK(r == CUDA_SUCCESS, "flash_bwd_tc: dq tensor map encode failed ", int(r));
   }

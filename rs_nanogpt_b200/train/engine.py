@@ -43,6 +43,9 @@ class TrainEngine:
         fused = comm == "fused" and self.dist.world_size() > 1 and store.device.type == "cuda"
         self.opt = GroupedAdamW(store, lrs, self.cfg.n_embd, wd, allocate_state=not fused)
         self.fused_ddp = None
+        # When a list, the overlapped fused step appends (start, end) CUDA
+        # events of its exposed communication tail (benchmark telemetry).
+        self.tail_events = None
         # Reads (and clears) the kernels' device error word; None on CPU.
         self.status_fn = None
         if store.device.type == "cuda":
@@ -117,7 +120,14 @@ class TrainEngine:
             if on_micro is not None:
                 on_micro(i)
         if overlap:
+            ev = None
+            if self.tail_events is not None:
+                ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                ev[0].record()
             self.fused_ddp.finish_step()
+            if ev is not None:
+                ev[1].record()
+                self.tail_events.append(ev)
             return StepStats(nll_sum, count)
         grad_scale = 1.0
         if targets_may_be_ignored:
