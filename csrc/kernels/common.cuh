@@ -17,7 +17,23 @@ constexpr uint32_t kSpinLimit = 1u << 26;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
 enum : int { kErrNone = 0, kErrTimeoutProducer = 1, kErrTimeoutMma = 2, kErrTimeoutEpilogue = 3,
-             kErrTimeoutOther = 4 };
+             kErrTimeoutOther = 4, kErrBounds = 5 };
+
+// Tile-index checks of the debug build (compiled with -DNANOGPT_DEBUG_BOUNDS,
+// the `_C_bounds` extension): NK_IN_BOUNDS(cond, err) records kErrBounds in
+// the error word when a TMA coordinate, bulk-copy offset or row index is out
+// of range or misaligned, and evaluates to false so the caller skips that
+// access instead of faulting. In the regular build it is the constant true
+// and costs nothing.
+#ifdef NANOGPT_DEBUG_BOUNDS
+__device__ __forceinline__ bool nk_bounds_ok(bool ok, int* err) {
+  if (!ok) atomicCAS(err, 0, kErrBounds);
+  return ok;
+}
+#define NK_IN_BOUNDS(cond, err) (::nk::nk_bounds_ok(bool(cond), (err)))
+#else
+#define NK_IN_BOUNDS(cond, err) true
+#endif
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -234,6 +250,19 @@ __device__ __forceinline__ void tmem_ld_32x32(uint32_t taddr, float (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Split form of tmem_ld_32x32: issue the load, then (after issuing others)
+// wait for all of this thread's outstanding tensor-memory loads. The wait
+// names the destination registers as read-write operands, so no use of them
+// can be scheduled before it.
+__device__ __forceinline__ void tmem_ld_32x32_issue(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31]) : : "memory");
 }
 
 // 32 lanes x 64 columns of fp32, the load and its completion wait in one

@@ -573,6 +573,7 @@ void flash_dsum(torch::Tensor out, torch::Tensor dout, torch::Tensor dsum, int64
 
 }  // namespace nk
 
+#ifndef NANOGPT_DEBUG_BOUNDS  // the bounds-checked debug extension does not carry the C entry point
 // ---------------------------------------------------------------------------------------------
 // Allocation-free C entry point (declared and documented in noalloc.h): the same
 // three backward kernels, with the D = rowsum(dO o O) scratch taken from a fixed
@@ -688,3 +689,4 @@ extern "C" __attribute__((visibility("default"))) int nanogpt_flash_attention_bw
   else flash_bwd_dkv_kernel<64><<<gk, 128, smk, stream>>>(kv);
   return cudaGetLastError() == cudaSuccess ? NANOGPT_NOALLOC_OK : NANOGPT_NOALLOC_ERR_CUDA;
 }
+#endif  // NANOGPT_DEBUG_BOUNDS

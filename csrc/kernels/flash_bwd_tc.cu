@@ -79,7 +79,12 @@ struct FbArgs {
   const float* rope_cos;
   const float* rope_sin;
   // Measurement switch (NANOGPT_FB_DEBUG; gives wrong gradients when set):
-  // bit 0 skips the dQ reduce-add, bit 1 replaces the softmax-gradient math by copies.
+  // bit 0 skips the dQ reduce-add, bit 1 replaces the softmax-gradient math by
+  // copies, bit 2 skips the dQ^T MMAs, bit 3 the dV / dK MMAs, bit 4 the S^T / dP^T MMAs,
+  // bit 5 makes the MMA warp skip its wait for the dQ^T drain, bit 6 skips the
+  // tensor-memory traffic of the softmax warps, bit 7 loads only the first
+  // stages' Q / dO (later stages are released without a copy), bit 8 skips the
+  // dK / dV write-out.
   int dbg;
 };
 
@@ -148,13 +153,19 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       mbar_arrive_expect_tx(kv_full, 2 * kKTile);
       for (int s = 0; s < 2; ++s)
         for (int r = 0; r < 2; ++r) {  // 64-row boxes: the second lands 8 KB into the sub-tile
+          if (!NK_IN_BOUNDS(kb * BK + 64 * r < a.T && b < a.B && xv + 64 * s < 3 * a.C, a.err)) continue;
           tma_load_3d(sK + s * kKSub + r * kQSub, &tm, kv_full, xk + 64 * s, kb * BK + 64 * r, b);
           tma_load_3d(sV + s * kKSub + r * kQSub, &tm, kv_full, xv + 64 * s, kb * BK + 64 * r, b);
         }
       for (int n = 0; n < nblk; ++n) {
         const int j = j0 + n, st = n % NS;
         if (!mbar_wait(&qd_empty[st], ((n / NS) & 1) ^ 1, kErrTimeoutProducer, a.err)) break;
+        if ((a.dbg & 128) && n >= NS) {
+          mbar_arrive(&qd_full[st]);
+          continue;
+        }
         mbar_arrive_expect_tx(&qd_full[st], 2 * kQTile + 2 * BQ * 4);
+        if (!NK_IN_BOUNDS(j * BQ + BQ <= a.T && xq + 128 <= a.C, a.err)) break;
         for (int s = 0; s < 2; ++s) {
           tma_load_3d(sQ + st * kQTile + s * kQSub, &tm, &qd_full[st], xq + 64 * s, j * BQ, b);
           tma_load_3d(sO + st * kQTile + s * kQSub, &tmo, &qd_full[st], h * HD + 64 * s, j * BQ, b);
@@ -177,14 +188,17 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
         const uint32_t q = smem_u32(sQ + st * kQTile), o = smem_u32(sO + st * kQTile);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
+          if (a.dbg & 16) break;
           const uint32_t ka = (kk >> 2) * kKSub + (kk & 3) * 32, qa = (kk >> 2) * kQSub + (kk & 3) * 32;
           umma_bf16(tmem + 64 * u, sw128_desc(k + ka, 16, 1024), sw128_desc(q + qa, 16, 1024), id_s, kk > 0);
         }
         // dP^T reuses the columns of dQ^T of block n - 2: wait until it was drained.
-        if (n >= 2 && !mbar_wait(&dq_free[u], ((n - 2) >> 1) & 1, kErrTimeoutMma, a.err)) return false;
+        if (n >= 2 && !(a.dbg & 32) && !mbar_wait(&dq_free[u], ((n - 2) >> 1) & 1, kErrTimeoutMma, a.err))
+          return false;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
+          if (a.dbg & 16) break;
           const uint32_t ka = (kk >> 2) * kKSub + (kk & 3) * 32, qa = (kk >> 2) * kQSub + (kk & 3) * 32;
           umma_bf16(tmem + 128 + 64 * u, sw128_desc(v + ka, 16, 1024), sw128_desc(o + qa, 16, 1024), id_s,
                     kk > 0);
@@ -201,12 +215,12 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
         const uint32_t q = smem_u32(sQ + st * kQTile), o = smem_u32(sO + st * kQTile);
         const uint32_t ds = smem_u32(sDs + u * kDsTile);
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk)  // dQ^T = K^T dS^T: contraction over the 128 keys
+        for (int kk = 0; kk < BK / 16 && !(a.dbg & 4); ++kk)  // dQ^T = K^T dS^T: contraction over the 128 keys
           umma_bf16(tmem + 128 + 64 * u, sw128_desc(k + kk * 2048, kKSub, 1024),
                     sw128_desc(ds + kk * 2048, kDsTile, 1024), id_q, kk > 0);
         umma_commit(&dq_full[u]);
 #pragma unroll
-        for (int kk = 0; kk < BQ / 16; ++kk) {  // contraction over the 64 queries
+        for (int kk = 0; kk < BQ / 16 && !(a.dbg & 8); ++kk) {  // contraction over the 64 queries
           // P^T is in tensor memory: 32 query columns of chunk c packed as bf16
           // pairs in TMEM columns [64u + 32c, 64u + 32c + 16) (written over S^T).
           umma_bf16_ts(tmem + 384, tmem + 64 * u + 32 * (kk >> 1) + 8 * (kk & 1),
@@ -233,9 +247,22 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       // dS^T tile u (read by dK / dQ of block n - 2) is free as well.
       if (!mbar_wait(&st_full[u], (n >> 1) & 1, kErrTimeoutEpilogue, a.err)) { ok = false; break; }
       tc_fence_after();
+      uint32_t sr[32], dr[32];  // both loads in flight, one wait
+      if (!(a.dbg & 64)) {
+        tmem_ld_32x32_issue(tmem + lanes + 64 * u + 32 * half, sr);
+        tmem_ld_32x32_issue(tmem + lanes + 128 + 64 * u + 32 * half, dr);
+        tmem_ld_wait(sr);
+        tmem_ld_wait(dr);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sr[i] = dr[i] = __float_as_uint(float(i));
+      }
       float s[32], dp[32];
-      tmem_ld_32x32(tmem + lanes + 64 * u + 32 * half, s);
-      tmem_ld_32x32(tmem + lanes + 128 + 64 * u + 32 * half, dp);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        s[i] = __uint_as_float(sr[i]);
+        dp[i] = __uint_as_float(dr[i]);
+      }
       const float* L = sL + st * BQ + 32 * half;
       const float* D = sD + st * BQ + 32 * half;
       const bool diag = n < BK / BQ;
@@ -259,7 +286,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
         dd[i / 2] = pack_bf16x2(gv[0], gv[1]);
         dd[i / 2 + 1] = pack_bf16x2(gv[2], gv[3]);
       }
-      tmem_st_32x16(tmem + lanes + 64 * u + 32 * half, pp);
+      if (!(a.dbg & 64)) tmem_st_32x16(tmem + lanes + 64 * u + 32 * half, pp);
       uint8_t* ds = sDs + u * kDsTile;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {  // 16-byte chunk 4 * half + c of row r, 128-byte swizzle
@@ -272,9 +299,9 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[u]);
     }
-    if (ok && mbar_wait(kv_done, 0, kErrTimeoutEpilogue, a.err)) {
+    if (ok && mbar_wait(kv_done, 0, kErrTimeoutEpilogue, a.err) && !(a.dbg & 256)) {
       tc_fence_after();
-      if (key < a.T && half == 1) {
+      if (key < a.T && half == 1 && NK_IN_BOUNDS(b < a.B && h < a.H, a.err)) {
         __nv_bfloat16* dv = a.dqkv + (long(b) * a.T + key) * 3 * a.C + 2 * a.C + h * HD;
 #pragma unroll 1
         for (int c = 0; c < HD / 32; ++c) {
@@ -391,9 +418,11 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       const int j = j0 + n, u = n & 1;
       if (!mbar_wait(&dq_full[u], (n >> 1) & 1, kErrTimeoutEpilogue, a.err)) break;
       tc_fence_after();
-      float x[2][32];
-      tmem_ld_32x32(tmem + lanes + 128 + 64 * u, x[0]);
-      tmem_ld_32x32(tmem + lanes + 128 + 64 * u + 32, x[1]);
+      uint32_t xr[2][32];
+      tmem_ld_32x32_issue(tmem + lanes + 128 + 64 * u, xr[0]);
+      tmem_ld_32x32_issue(tmem + lanes + 128 + 64 * u + 32, xr[1]);
+      tmem_ld_wait(xr[0]);
+      tmem_ld_wait(xr[1]);
       // The dQ^T columns are free for the scores of block n + 2.
       tc_fence_before();
       __syncwarp();
@@ -405,10 +434,11 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
         if (lane == 0 && chunks >= 2) bulk_wait_read<1>();  // this buffer's previous reduce has read it
         __syncwarp();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) buf[i * 32 + lane] = x[c][i] * a.scale;
+        for (int i = 0; i < 32; ++i) buf[i * 32 + lane] = __uint_as_float(xr[c][i]) * a.scale;
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) {
+          if (NK_IN_BOUNDS(j * BQ + 32 * c < a.T && h * HD + quarter * 32 < a.C, a.err))
           asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];"
                        ::"l"(&tmq), "r"(smem_u32(buf)), "r"(h * HD + quarter * 32), "r"(b * a.T + j * BQ + 32 * c)
                        : "memory");

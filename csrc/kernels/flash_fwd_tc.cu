@@ -105,7 +105,9 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
   const uint32_t tmem = *tmem_slot;  // S0 @0, S1 @128, O0 @256, O1 @384
 
   if (warp == 0) {
-    if (lane == 0) {
+    // (The debug build skips the loads of an out-of-range tile; the waits on
+    // them then run out and the CTA still reaches the final barrier.)
+    if (lane == 0 && NK_IN_BOUNDS(q0 + 2 * BM <= a.T && b < a.B && xv + 128 <= 3 * a.C, a.err)) {
       mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
       for (int t = 0; t < 2; ++t)
         for (int s = 0; s < 2; ++s)
@@ -252,7 +254,7 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t]);
     }
-    if (ok && mbar_wait(&o_done[t], (nblk - 1) & 1, kErrTimeoutEpilogue, a.err)) {
+    if (ok && mbar_wait(&o_done[t], (nblk - 1) & 1, kErrTimeoutEpilogue, a.err) && NK_IN_BOUNDS(qrow < a.T, a.err)) {
       tc_fence_after();
       const float inv = 1.f / l;
       __nv_bfloat16* orow = a.out + (long(b) * a.T + qrow) * a.ld_out + h * HD;

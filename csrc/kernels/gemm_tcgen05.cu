@@ -235,11 +235,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         unit_coords(args, blockIdx.x, m, n, kb0, kb1);
         for (int kb = kb0; kb < kb1 && pre < STAGES; ++kb, ++pre) {
           mbar_arrive_expect_tx(&full_bar[pre], S::kStageBytes);
-          tma_load_2d(smem + pre * S::kStageBytes, &tmA, &full_bar[pre], kb * BK, m * BM);
+          if (NK_IN_BOUNDS(kb * BK < args.K && m * BM < args.M + 2 * BM, args.err))
+            tma_load_2d(smem + pre * S::kStageBytes, &tmA, &full_bar[pre], kb * BK, m * BM);
         }
       }
       pdl_wait();
-      auto load = [&](void* dst, const CUtensorMap* map, int stage_, int c0, int c1) {
+      // (c0, c1) of a bf16 map whose extents are (n0, n1): the inner coordinate
+      // must be 16-byte aligned. Boxes of a ragged last tile may start past the
+      // extent (TMA fills zeros); the debug build checks that a box starts no
+      // further out than one tile.
+      auto load = [&](void* dst, const CUtensorMap* map, int stage_, int c0, int c1, int n0, int n1) {
+        if (!NK_IN_BOUNDS(c0 % 8 == 0 && c0 >= 0 && c1 >= 0 && c0 < n0 + BK && c1 < n1 + 2 * BM, args.err)) return;
         if (PAIR) tma_load_2d_pair(dst, map, map_to_cta(&full_bar[stage_], 0), c0, c1);
         else tma_load_2d(dst, map, &full_bar[stage_], c0, c1);
       };
@@ -256,17 +262,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!mbar_wait(&empty_bar[stage], phase ^ 1, kErrTimeoutProducer, args.err)) { ok = false; break; }
             if (leader) mbar_arrive_expect_tx(&full_bar[stage], (PAIR ? 2 : 1) * S::kStageBytes);
             if (!args.a_mn_major) {
-              load(sa, &tmA, stage, kb * BK, arow);
+              load(sa, &tmA, stage, kb * BK, arow, args.K, args.M);
             } else {
 #pragma unroll
-              for (int j = 0; j < BM / 64; ++j) load(sa + j * 8192, &tmA, stage, arow + 64 * j, kb * BK);
+              for (int j = 0; j < BM / 64; ++j) load(sa + j * 8192, &tmA, stage, arow + 64 * j, kb * BK, args.M, args.K);
             }
           }
           if (!args.b_mn_major) {
-            load(sb, &tmB, stage, kb * BK, brow);
+            load(sb, &tmB, stage, kb * BK, brow, args.K, args.N);
           } else {
 #pragma unroll
-            for (int j = 0; j < S::kBRows / 64; ++j) load(sb + j * 8192, &tmB, stage, brow + 64 * j, kb * BK);
+            for (int j = 0; j < S::kBRows / 64; ++j) load(sb + j * 8192, &tmB, stage, brow + 64 * j, kb * BK, args.N, args.K);
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -341,7 +347,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) {
         mbar_arrive_expect_tx(&aux_bar[2 * ew + (ckk & 1)], kStageBufBytes);
-        tma_load_2d(bufX(ckk), &tmX, &aux_bar[2 * ew + (ckk & 1)], col, row);
+        if (NK_IN_BOUNDS(col % 8 == 0 && col >= 0 && col < args.N && row >= 0 && row < args.M + BM, args.err))
+          tma_load_2d(bufX(ckk), &tmX, &aux_bar[2 * ew + (ckk & 1)], col, row);
       }
     };
     bool ok = true;
@@ -403,7 +410,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_proxy_async();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmC, sb, colb + c4 * 32, row0);
+            if (NK_IN_BOUNDS(row0 >= 0 && row0 < args.M + BM && colb + c4 * 32 < args.N, args.err))
+              tma_store_2d(&tmC, sb, colb + c4 * 32, row0);
             bulk_commit();
           }
           ++ck;
@@ -472,8 +480,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmC, bufS(ck), col0, row0);
-          if (keep_h) tma_store_2d(&tmX, bufX(ck), col0, row0);
+          // (Rows past M inside the last tile are clipped by the TMA store.)
+          if (NK_IN_BOUNDS(col0 % 8 == 0 && col0 >= 0 && col0 < args.N && row0 >= 0 && row0 < args.M + BM, args.err)) {
+            tma_store_2d(&tmC, bufS(ck), col0, row0);
+            if (keep_h) tma_store_2d(&tmX, bufX(ck), col0, row0);
+          }
           bulk_commit();
         }
         ++ck;

@@ -10,8 +10,6 @@ reuses the array the first one left behind). It lives in its own file, named
 to be collected last.
 """
 import ctypes
-import glob
-import os
 
 import pytest
 import torch
@@ -20,11 +18,8 @@ pytestmark = pytest.mark.gpu
 
 
 def _lib():
-    import rs_nanogpt_b200
-    pkg = os.path.dirname(rs_nanogpt_b200.__file__)
-    paths = glob.glob(os.path.join(pkg, "_C*.so"))
-    assert paths, "rs_nanogpt_b200._C is not built"
-    lib = ctypes.CDLL(paths[0])
+    from rs_nanogpt_b200 import _C  # the regular extension (not the _C_bounds debug build)
+    lib = ctypes.CDLL(_C.__file__)
     fn = lib.nanogpt_flash_attention_bwd_noalloc
     fn.restype = ctypes.c_int
     fn.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int] * 4 + [ctypes.c_void_p]
