@@ -36,6 +36,7 @@ void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torc
 void flash_bwd_prep(torch::Tensor out, torch::Tensor dout, torch::Tensor dsum, torch::Tensor dq_acc, int64_t B,
                     int64_t T, int64_t H);
 bool flash_bwd_tc_supported(int64_t T, int64_t HD);
+torch::Tensor flash_bwd_trace();
 void gemm_qkv_rope(torch::Tensor x, torch::Tensor w, torch::Tensor qkv, torch::Tensor rstd, torch::Tensor cos_t,
                    torch::Tensor sin_t, int64_t T, int64_t H, double eps);
 void kv_rope_append(torch::Tensor qkv, torch::Tensor k_cache, torch::Tensor v_cache, c10::optional<torch::Tensor> pos,
@@ -79,6 +80,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("prepared") = false);
   m.def("flash_bwd_prep", &nk::flash_bwd_prep);
   m.def("flash_bwd_tc_supported", &nk::flash_bwd_tc_supported);
+  m.def("flash_bwd_trace", &nk::flash_bwd_trace, "timeline of the first CTA of the last traced backward (measurement)");
   m.def("flash_fwd_tc_supported", &nk::flash_fwd_tc_supported);
   m.def("ddp_barrier", &nk::ddp_barrier);
   m.def("ddp_rs_adam_ag", &nk::ddp_rs_adam_ag);

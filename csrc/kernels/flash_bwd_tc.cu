@@ -47,13 +47,13 @@ namespace nk {
 
 namespace fb {
 constexpr int HD = 128, BK = 128, BQ = 64, NS = 3;
+constexpr int kStage = 32 * 32 * 4;      // 4 KB: one drain warp's 32 x 32 fp32 dQ chunk
 constexpr int kThreads = 448;            // 2 + 8 softmax + 4 drain warps
 constexpr int kKTile = 128 * 128 * 2;    // 32 KB: K or V (two 64-column sub-tiles)
 constexpr int kKSub = 128 * 64 * 2;      // 16 KB
 constexpr int kQTile = BQ * 128 * 2;     // 16 KB: one query block of Q or dO
 constexpr int kQSub = BQ * 64 * 2;       // 8 KB
 constexpr int kDsTile = 128 * BQ * 2;    // 16 KB: dS^T [key][query], one 128-byte-row sub-tile
-constexpr int kStage = 32 * 32 * 4;      // 4 KB: one drain warp's 32 x 32 fp32 dQ chunk
 constexpr int kOffK = 0, kOffV = kKTile, kOffQ = 2 * kKTile, kOffO = kOffQ + NS * kQTile,
               kOffDs = kOffO + NS * kQTile, kOffStage = kOffDs + 2 * kDsTile,
               kOffLD = kOffStage + 4 * 2 * kStage, kOffBar = kOffLD + NS * 2 * BQ * 4;
@@ -79,18 +79,30 @@ struct FbArgs {
   const float* rope_cos;
   const float* rope_sin;
   // Measurement switch (NANOGPT_FB_DEBUG; gives wrong gradients when set):
-  // bit 0 skips the dQ reduce-add, bit 1 replaces the softmax-gradient math by
-  // copies, bit 2 skips the dQ^T MMAs, bit 3 the dV / dK MMAs, bit 4 the S^T / dP^T MMAs,
-  // bit 5 makes the MMA warp skip its wait for the dQ^T drain, bit 6 skips the
-  // tensor-memory traffic of the softmax warps, bit 7 loads only the first
-  // stages' Q / dO (later stages are released without a copy), bit 8 skips the
-  // dK / dV write-out.
+  // bit 0 skips the dQ reduce-add, bit 2 skips the dQ^T MMAs, bit 3 the dV / dK MMAs, bit 4 the S^T / dP^T MMAs,
+  // bit 5 makes the MMA warp skip its wait for the dQ^T drain, bit 7 loads only
+  // the first stages' Q / dO (later stages are released without a copy), bit 8
+  // skips the dK / dV write-out, bit 9 records a timeline (g_fb_trace), bit 13
+  // adds dQ with red.global.add from registers instead of TMA reduce-adds.
   int dbg;
 };
 
+// Timeline of the first CTA (measurement switch NANOGPT_FB_DEBUG bit 9): per
+// query block n, clock64 stamps at slot [n * 16 + k]: k = 0 scores of n + 1
+// issued, 1 P of n ready (MMA warp), 2 gradient MMAs of n issued, 3 scores of n
+// seen by the softmax warps, 4 softmax of n done, 5 dQ^T of n seen by the
+// drain, 6 dQ^T of n read out; softmax internals 8 tensor-memory loads done,
+// 9 math done, 10 P^T stored to tensor memory, 11 dS^T stored to shared memory.
+__device__ long long g_fb_trace[64 * 16];
+
+__device__ __forceinline__ void fb_stamp(const FbArgs& a, int n, int k) {
+  if ((a.dbg & 512) && blockIdx.x == 0 && blockIdx.y == 0 && n < 64) g_fb_trace[n * 16 + k] = clock64();
+}
+
 __global__ void __launch_bounds__(fb::kThreads, 1)
     flash_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tmo,
-                        const __grid_constant__ CUtensorMap tmq, const FbArgs a) {
+                        const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmd,
+                        const FbArgs a) {
   using namespace fb;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw;
@@ -108,13 +120,14 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* kv_full = bars + 0;
   uint64_t* qd_full = bars + 1;    // [NS]
-  uint64_t* qd_empty = bars + 4;   // [NS]
-  uint64_t* st_full = bars + 7;    // [2] S^T and dP^T of a block are in tensor memory
-  uint64_t* p_full = bars + 9;     // [2] P^T (tensor memory) and dS^T (shared memory) written
-  uint64_t* dq_full = bars + 11;   // [2] dQ^T of a block is in tensor memory
-  uint64_t* dq_free = bars + 13;   // [2] ... and has been read out by the drain warps
-  uint64_t* kv_done = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* qd_empty = bars + 1 + NS;   // [NS]
+  uint64_t* st_full = bars + 1 + 2 * NS;    // [2] S^T and dP^T of a block are in tensor memory
+  uint64_t* p_full = st_full + 2;     // [2] P^T (tensor memory) and dS^T (shared memory) written
+  uint64_t* dq_full = p_full + 2;   // [2] dQ^T of a block is in tensor memory
+  uint64_t* dq_free = dq_full + 2;   // [2] ... and has been read out by the drain warps
+  uint64_t* kv_done = dq_free + 2;
+  uint64_t* epi_full = kv_done + 1;  // all 8 softmax warps staged their dK / dV rows
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_full + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int kb = blockIdx.x;  // key block; low blocks have the most query blocks
@@ -137,6 +150,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       mbar_init(&dq_free[i], 4);
     }
     mbar_init(kv_done, 1);
+    mbar_init(epi_full, 8);
     fence_barrier_init();
     prefetch_tmap(&tm);
     prefetch_tmap(&tmo);
@@ -210,7 +224,9 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       for (int n = 0; n < nblk && ok; ++n) {
         const int st = n % NS, u = n & 1;
         if (n + 1 < nblk && !scores(n + 1)) break;
+        fb_stamp(a, n, 0);
         if (!mbar_wait(&p_full[u], (n >> 1) & 1, kErrTimeoutMma, a.err)) break;
+        fb_stamp(a, n, 1);
         tc_fence_after();
         const uint32_t q = smem_u32(sQ + st * kQTile), o = smem_u32(sO + st * kQTile);
         const uint32_t ds = smem_u32(sDs + u * kDsTile);
@@ -229,6 +245,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
                     (n > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&qd_empty[st]);  // Q_j / dO_j / their LSE and D rows are no longer read
+        fb_stamp(a, n, 2);
       }
       umma_commit(kv_done);
     }
@@ -243,50 +260,56 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
     bool ok = true;
     for (int n = 0; n < nblk && ok; ++n) {
       const int j = j0 + n, u = n & 1, st = n % NS;
+      // The block's lse2 / D rows arrived with its Q tile (long before its
+      // scores): fetch this warp's 32 + 32 of them into registers now, so the
+      // shared-memory loads (which queue behind the tensor cores' operand
+      // reads) complete while the warp waits for the scores.
+      float lv[32], dv[32];
+      if (!mbar_wait(&qd_full[st], (n / NS) & 1, kErrTimeoutEpilogue, a.err)) { ok = false; break; }
+      {
+        const float4* L4 = reinterpret_cast<const float4*>(sL + st * BQ + 32 * half);
+        const float4* D4 = reinterpret_cast<const float4*>(sD + st * BQ + 32 * half);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 l4 = L4[i], d4 = D4[i];
+          lv[4 * i] = l4.x; lv[4 * i + 1] = l4.y; lv[4 * i + 2] = l4.z; lv[4 * i + 3] = l4.w;
+          dv[4 * i] = d4.x; dv[4 * i + 1] = d4.y; dv[4 * i + 2] = d4.z; dv[4 * i + 3] = d4.w;
+        }
+      }
       // st_full of block n is committed after every MMA of block n - 2, so
       // dS^T tile u (read by dK / dQ of block n - 2) is free as well.
       if (!mbar_wait(&st_full[u], (n >> 1) & 1, kErrTimeoutEpilogue, a.err)) { ok = false; break; }
+      if (warp == 2 && lane == 0) fb_stamp(a, n, 3);
       tc_fence_after();
-      uint32_t sr[32], dr[32];  // both loads in flight, one wait
-      if (!(a.dbg & 64)) {
-        tmem_ld_32x32_issue(tmem + lanes + 64 * u + 32 * half, sr);
-        tmem_ld_32x32_issue(tmem + lanes + 128 + 64 * u + 32 * half, dr);
-        tmem_ld_wait(sr);
-        tmem_ld_wait(dr);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) sr[i] = dr[i] = __float_as_uint(float(i));
-      }
-      float s[32], dp[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        s[i] = __uint_as_float(sr[i]);
-        dp[i] = __uint_as_float(dr[i]);
-      }
-      const float* L = sL + st * BQ + 32 * half;
-      const float* D = sD + st * BQ + 32 * half;
       const bool diag = n < BK / BQ;
       const int q0 = j * BQ + 32 * half;
       uint32_t pp[16], dd[16];
+      // Two halves of 16 columns keep the live registers under the budget.
 #pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        const float4 l4 = *reinterpret_cast<const float4*>(L + i);
-        const float4 d4 = *reinterpret_cast<const float4*>(D + i);
-        const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
-        float pv[4], gv[4];
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t sr[16], dr[16];  // both loads in flight, one wait
+        tmem_ld_32x16_issue(tmem + lanes + 64 * u + 32 * half + 16 * hh, sr);
+        tmem_ld_32x16_issue(tmem + lanes + 128 + 64 * u + 32 * half + 16 * hh, dr);
+        tmem_ld_wait16(sr);
+        tmem_ld_wait16(dr);
+        if (warp == 2 && lane == 0 && hh == 0) fb_stamp(a, n, 8);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          if (a.dbg & 2) { pv[e] = s[i + e]; gv[e] = dp[i + e]; continue; }
-          pv[e] = exp2f(fmaf(s[i + e], a.sl2, -lv[e]));
-          if (diag && (q0 + i + e) < key) pv[e] = 0.f;
-          gv[e] = pv[e] * (dp[i + e] - dv4[e]);
+        for (int i = 0; i < 16; i += 2) {
+          float pv[2], gv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int c = 16 * hh + i + e;
+            pv[e] = ex2_approx(fmaf(__uint_as_float(sr[i + e]), a.sl2, -lv[c]));
+            if (diag && (q0 + c) < key) pv[e] = 0.f;
+            gv[e] = pv[e] * (__uint_as_float(dr[i + e]) - dv[c]);
+          }
+          pp[(16 * hh + i) / 2] = pack_bf16x2(pv[0], pv[1]);
+          dd[(16 * hh + i) / 2] = pack_bf16x2(gv[0], gv[1]);
         }
-        pp[i / 2] = pack_bf16x2(pv[0], pv[1]);
-        pp[i / 2 + 1] = pack_bf16x2(pv[2], pv[3]);
-        dd[i / 2] = pack_bf16x2(gv[0], gv[1]);
-        dd[i / 2 + 1] = pack_bf16x2(gv[2], gv[3]);
       }
-      if (!(a.dbg & 64)) tmem_st_32x16(tmem + lanes + 64 * u + 32 * half, pp);
+      if (warp == 2 && lane == 0) fb_stamp(a, n, 9);
+      tmem_st_32x16(tmem + lanes + 64 * u + 32 * half, pp);
+      if (warp == 2 && lane == 0) fb_stamp(a, n, 10);
       uint8_t* ds = sDs + u * kDsTile;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {  // 16-byte chunk 4 * half + c of row r, 128-byte swizzle
@@ -294,37 +317,47 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
         *reinterpret_cast<uint4*>(ds + r * 128 + ((cc ^ (r & 7)) << 4)) =
             make_uint4(dd[4 * c], dd[4 * c + 1], dd[4 * c + 2], dd[4 * c + 3]);
       }
+      if (warp == 2 && lane == 0) fb_stamp(a, n, 11);
       fence_proxy_async();
       tc_fence_before();
       __syncwarp();
+      if (warp == 2 && lane == 0) fb_stamp(a, n, 4);
       if (lane == 0) mbar_arrive(&p_full[u]);
     }
-    if (ok && mbar_wait(kv_done, 0, kErrTimeoutEpilogue, a.err) && !(a.dbg & 256)) {
+    if (ok && mbar_wait(kv_done, 0, kErrTimeoutEpilogue, a.err) && !(a.dbg & 256) &&
+        NK_IN_BOUNDS(key < a.T && b < a.B && h < a.H, a.err)) {
       tc_fence_after();
-      if (key < a.T && half == 1 && NK_IN_BOUNDS(b < a.B && h < a.H, a.err)) {
-        __nv_bfloat16* dv = a.dqkv + (long(b) * a.T + key) * 3 * a.C + 2 * a.C + h * HD;
+      // dK (warps of chunk 0) and dV (chunk 1) are staged as bf16 tiles in
+      // the now idle Q / dO stages, in the 128-byte-swizzled layout of the
+      // tensor map's 64 x 64 boxes, and written with TMA tensor stores (one
+      // thread per key row writing its own row would scatter every store
+      // instruction over 32 rows).
+      uint8_t* stg = smem + kOffQ + half * kKTile;
+      auto slot = [&](uint8_t* base, int col) {  // 16-byte chunk holding columns [col, col + 8) of row r
+        const int ch = col >> 3;
+        return base + (ch >> 3) * kKSub + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
+      };
+      auto put8 = [&](int col, const float* v) {
+        *reinterpret_cast<uint4*>(slot(stg, col)) =
+            make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                       pack_bf16x2(v[6], v[7]));
+      };
+      if (half == 1) {
 #pragma unroll 1
         for (int c = 0; c < HD / 32; ++c) {
           float y[32];
           tmem_ld_32x32(tmem + lanes + 384 + c * 32, y);
 #pragma unroll
-          for (int u = 0; u < 4; ++u)
-            *reinterpret_cast<uint4*>(dv + c * 32 + u * 8) = make_uint4(
-                pack_bf16x2(y[8 * u], y[8 * u + 1]), pack_bf16x2(y[8 * u + 2], y[8 * u + 3]),
-                pack_bf16x2(y[8 * u + 4], y[8 * u + 5]), pack_bf16x2(y[8 * u + 6], y[8 * u + 7]));
+          for (int u = 0; u < 4; ++u) put8(c * 32 + u * 8, y + 8 * u);
         }
-      } else if (key < a.T) {
-        __nv_bfloat16* dk = a.dqkv + (long(b) * a.T + key) * 3 * a.C + a.C + h * HD;
+      } else {
         // dK = scale * acc; with the RoPE fold, d/dx of y = rms(rope(x)):
         // dr = r (g - y <g, y> / D), then the transposed rotation of the
-        // pairs (i, i + 64). Columns are processed 32 + 32 at a time.
+        // pairs (i, i + 64). y (the stored normalized k) is this CTA's K tile,
+        // already in shared memory. Columns are processed 32 + 32 at a time.
         const long row = long(b) * a.T + key;
-        const __nv_bfloat16* yk = a.qkv + row * 3 * a.C + a.C + h * HD;
-        // Each lane reads its own row of y and of the RoPE tables: 16-byte
-        // vector loads (8 bf16 / 4 fp32) keep the warp's cache-line requests
-        // per column few.
-        auto load8 = [](const __nv_bfloat16* p, float (&v)[8]) {
-          const uint4 w = *reinterpret_cast<const uint4*>(p);
+        auto get8 = [&](int col, float (&v)[8]) {
+          const uint4 w = *reinterpret_cast<const uint4*>(slot(sK, col));
           const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
@@ -333,9 +366,9 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
             v[2 * k + 1] = f.y;
           }
         };
-        float dot = 0.f, r = 0.f;
+        float dot = 0.f, rr = 0.f;
         if (a.rope_rstd) {
-          r = a.rope_rstd[row * 2 * a.H + a.H + h];
+          rr = a.rope_rstd[row * 2 * a.H + a.H + h];
 #pragma unroll 1
           for (int c = 0; c < HD / 32; ++c) {
             float x[32];
@@ -343,7 +376,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               float y[8];
-              load8(yk + c * 32 + u * 8, y);
+              get8(c * 32 + u * 8, y);
 #pragma unroll
               for (int k = 0; k < 8; ++k) dot += y[k] * x[u * 8 + k];
             }
@@ -361,8 +394,8 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
           for (int u = 0; u < 4; ++u) {
             float y1[8], y2[8], cs[8], sn[8];
             if (a.rope_rstd) {
-              load8(yk + c * 32 + u * 8, y1);
-              load8(yk + 64 + c * 32 + u * 8, y2);
+              get8(c * 32 + u * 8, y1);
+              get8(64 + c * 32 + u * 8, y2);
 #pragma unroll
               for (int k = 0; k < 8; k += 4) {
                 const float4 c4 = __ldg(reinterpret_cast<const float4*>(crow + c * 32 + u * 8 + k));
@@ -376,7 +409,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
               const int i = u * 8 + k;
               float g1 = x1[i] * a.scale, g2 = x2[i] * a.scale;
               if (a.rope_rstd) {
-                const float d1 = r * (g1 - y1[k] * dot), d2 = r * (g2 - y2[k] * dot);
+                const float d1 = rr * (g1 - y1[k] * dot), d2 = rr * (g2 - y2[k] * dot);
                 g1 = d1 * cs[k] - d2 * sn[k];  // dx1 = dy1 cos - dy2 sin
                 g2 = d1 * sn[k] + d2 * cs[k];  // dx2 = dy1 sin + dy2 cos
               }
@@ -386,21 +419,22 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
           }
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            *reinterpret_cast<uint4*>(dk + c * 32 + u * 8) =
-                make_uint4(pack_bf16x2(x1[8 * u], x1[8 * u + 1]), pack_bf16x2(x1[8 * u + 2], x1[8 * u + 3]),
-                           pack_bf16x2(x1[8 * u + 4], x1[8 * u + 5]), pack_bf16x2(x1[8 * u + 6], x1[8 * u + 7]));
-            *reinterpret_cast<uint4*>(dk + 64 + c * 32 + u * 8) =
-                make_uint4(pack_bf16x2(x2[8 * u], x2[8 * u + 1]), pack_bf16x2(x2[8 * u + 2], x2[8 * u + 3]),
-                           pack_bf16x2(x2[8 * u + 4], x2[8 * u + 5]), pack_bf16x2(x2[8 * u + 6], x2[8 * u + 7]));
+            put8(c * 32 + u * 8, x1 + 8 * u);
+            put8(64 + c * 32 + u * 8, x2 + 8 * u);
           }
         }
-      } else {
-        // Lanes past the sequence still take part in the warp-collective loads.
-#pragma unroll 1
-        for (int c = 0; c < HD / 32; ++c) {
-          float x[32];
-          tmem_ld_32x32(tmem + lanes + (half ? 384 : 256) + c * 32, x);
-        }
+      }
+      fence_proxy_async();  // the staged tiles are read by the TMA (async proxy)
+      __syncwarp();
+      if (lane == 0) mbar_arrive(epi_full);
+      if (warp == 2 && lane == 0 && mbar_wait(epi_full, 0, kErrTimeoutEpilogue, a.err)) {
+        for (int t = 0; t < 2; ++t)  // t = 0: dK, 1: dV
+          for (int sub = 0; sub < 2; ++sub)
+            for (int rh = 0; rh < 2; ++rh)
+              tma_store_3d(&tmd, smem + kOffQ + t * kKTile + sub * kKSub + rh * kQSub, (1 + t) * a.C + h * HD + 64 * sub,
+                           kb * BK + 64 * rh, b);
+        bulk_commit();
+        bulk_wait<0>();  // shared memory must stay valid until the stores are done
       }
     }
   } else {
@@ -417,6 +451,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
     for (int n = 0; n < nblk; ++n) {
       const int j = j0 + n, u = n & 1;
       if (!mbar_wait(&dq_full[u], (n >> 1) & 1, kErrTimeoutEpilogue, a.err)) break;
+      if (warp == 10 && lane == 0) fb_stamp(a, n, 5);
       tc_fence_after();
       uint32_t xr[2][32];
       tmem_ld_32x32_issue(tmem + lanes + 128 + 64 * u, xr[0]);
@@ -427,7 +462,16 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&dq_free[u]);
+      if (warp == 10 && lane == 0) fb_stamp(a, n, 6);
       if (a.dbg & 1) continue;
+      if (a.dbg & 8192) {  // measurement: coalesced red.global.add from registers, no staging
+        float* dst = a.dq_acc + (long(b) * a.T + j * BQ) * a.C + h * HD + quarter * 32 + lane;
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) atomicAdd(dst + long(32 * c + i) * a.C, __uint_as_float(xr[c][i]) * a.scale);
+        continue;
+      }
 #pragma unroll
       for (int c = 0; c < 2; ++c, ++chunks) {
         float* buf = stage + (chunks & 1) * (kStage / 4);
@@ -493,6 +537,14 @@ __global__ void dq_finish_kernel(const float* __restrict__ acc, __nv_bfloat16* _
   }
   *reinterpret_cast<uint2*>(dqkv + row * 3 * C + h * 128 + lane * 4) =
       make_uint2(pack_bf16x2(g[0], g[1]), pack_bf16x2(g[2], g[3]));
+}
+
+// The timeline written under NANOGPT_FB_DEBUG bit 9 (see g_fb_trace).
+torch::Tensor flash_bwd_trace() {
+  auto out = torch::zeros({64 * 16}, torch::dtype(torch::kInt64));
+  TORCH_CHECK(cudaMemcpyFromSymbol(out.data_ptr(), g_fb_trace, sizeof(long long) * 64 * 16) == cudaSuccess,
+              "flash_bwd_trace: copy failed");
+  return out;
 }
 
 bool flash_bwd_tc_supported(int64_t T, int64_t HD) { return HD == 128 && T % 128 == 0; }
@@ -596,7 +648,8 @@ void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torc
     configured = true;
   }
   dim3 grid(unsigned(T / BK), unsigned(B * H));
-  flash_bwd_tc_kernel<<<grid, kThreads, kSmem, stream>>>(tm, tmo, tmq, a);
+  CUtensorMap tmd = seq_map_3d(dqkv.data_ptr(), B, T, 3 * C);
+  flash_bwd_tc_kernel<<<grid, kThreads, kSmem, stream>>>(tm, tmo, tmq, tmd, a);
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "flash_bwd_tc launch failed");
   const long items = B * T * H;
   dq_finish_kernel<<<unsigned((items + 7) / 8), 256, 0, stream>>>(a.dq_acc, a.dqkv, B * T, int(T), int(H), int(C),
