@@ -17,6 +17,9 @@ void embedding_fwd(torch::Tensor idx, torch::Tensor wte, torch::Tensor out);
 void embedding_bwd(torch::Tensor idx, torch::Tensor dx, torch::Tensor grad);
 void softmax_xent(torch::Tensor logits, torch::Tensor targets, c10::optional<torch::Tensor> nll, double grad_scale,
                   bool write_grad);
+void xent_from_stats(torch::Tensor logits, torch::Tensor stats, torch::Tensor targets,
+                     c10::optional<torch::Tensor> nll, double grad_scale, bool write_grad);
+void gemm_logits_stats(torch::Tensor x, torch::Tensor w, torch::Tensor logits, torch::Tensor stats);
 void adamw_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, c10::optional<torch::Tensor> work,
                 double lr, double b1, double b2, double eps, double wd, int64_t step, double grad_scale);
 void sumsq(torch::Tensor x, torch::Tensor out);
@@ -26,7 +29,8 @@ void flash_bwd(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch::
 void ddp_barrier(int64_t pads_dev, int64_t rank, int64_t world, int64_t epoch);
 void ddp_rs_adam_ag(int64_t grads_dev, int64_t works_dev, int64_t world, torch::Tensor master, torch::Tensor m,
                     torch::Tensor v, int64_t shard_lo, int64_t shard_hi, torch::Tensor groups, double grad_scale,
-                    c10::optional<torch::Tensor> sumsq, int64_t mv_base);
+                    c10::optional<torch::Tensor> sumsq, int64_t mv_base, int64_t mc_grad, int64_t mc_work,
+                    int64_t max_ctas);
 void flash_fwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor lse, int64_t B, int64_t T, int64_t H);
 bool flash_fwd_tc_supported(int64_t T, int64_t HD);
 void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch::Tensor lse, torch::Tensor dsum,
@@ -69,6 +73,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding_fwd", &nk::embedding_fwd);
   m.def("embedding_bwd", &nk::embedding_bwd);
   m.def("softmax_xent", &nk::softmax_xent);
+  m.def("xent_from_stats", &nk::xent_from_stats);
+  m.def("gemm_logits_stats", &nk::gemm_logits_stats);
   m.def("adamw_step", &nk::adamw_step);
   m.def("sumsq", &nk::sumsq);
   m.def("flash_fwd", &nk::flash_fwd);
@@ -83,7 +89,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_bwd_trace", &nk::flash_bwd_trace, "timeline of the first CTA of the last traced backward (measurement)");
   m.def("flash_fwd_tc_supported", &nk::flash_fwd_tc_supported);
   m.def("ddp_barrier", &nk::ddp_barrier);
-  m.def("ddp_rs_adam_ag", &nk::ddp_rs_adam_ag);
+  m.def("ddp_rs_adam_ag", &nk::ddp_rs_adam_ag, py::arg("grads_dev"), py::arg("works_dev"), py::arg("world"),
+        py::arg("master"), py::arg("m"), py::arg("v"), py::arg("shard_lo"), py::arg("shard_hi"), py::arg("groups"),
+        py::arg("grad_scale"), py::arg("sumsq"), py::arg("mv_base") = 0, py::arg("mc_grad") = 0,
+        py::arg("mc_work") = 0, py::arg("max_ctas") = 0);
   m.def("kv_rope_append", &nk::kv_rope_append);
   m.def("decode_attention", &nk::decode_attention);
   m.def("sample_tokens", &nk::sample_tokens);

@@ -19,6 +19,10 @@
 // weights). Its waits are bounded: on timeout it records an error code and
 // returns instead of hanging.
 //
+// With NVLink SHARP available (multicast objects bound to the symmetric
+// buffers) a second kernel does the same step with multimem.ld_reduce /
+// multimem.st through the switch instead of per-peer loads and stores.
+//
 // Replaces rs-nanogpt's per-parameter NCCL AllReduce(Avg) followed by
 // candle's AdamW (src/train/dist.rs:327-347, src/train/optim.rs:146-150).
 #include <ATen/cuda/CUDAContext.h>
@@ -133,6 +137,82 @@ __global__ void __launch_bounds__(256) ddp_rs_adam_ag_kernel(const DdpArgs a) {
   }
 }
 
+// NVLS (NVLink SHARP) variant: the switch does the reduction and the
+// replication. For each 4-element vector of this rank's shard one
+// multimem.ld_reduce on the gradient buffer's multicast address returns the
+// sum over all ranks (inbound traffic: the shard once, instead of world - 1
+// peer copies of it), and one multimem.st on the working-copy buffer's
+// multicast address writes the new bf16 weights into every rank's copy
+// (outbound: the shard once). Rank order of the sum is the switch's; the
+// AdamW math is the same as in the P2P kernel.
+__device__ __forceinline__ float4 multimem_ld_add_v4(const float* mc) {
+  float4 r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "l"(mc)
+               : "memory");
+  return r;
+}
+__device__ __forceinline__ void multimem_st_v2(__nv_bfloat16* mc, uint2 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v2.f32 [%0], {%1, %2};" ::"l"(mc), "f"(__uint_as_float(v.x)),
+               "f"(__uint_as_float(v.y))
+               : "memory");
+}
+// Accesses through the multicast address alias the unicast buffers that the
+// other kernels use; order the two views.
+__device__ __forceinline__ void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
+
+__global__ void __launch_bounds__(256) ddp_rs_adam_ag_nvls_kernel(const DdpArgs a, const float* mc_grad,
+                                                                   __nv_bfloat16* mc_work) {
+  __shared__ float red[8];
+  fence_proxy_alias();
+  float ss = 0.f;
+  const long n4 = (a.shard_hi - a.shard_lo) / 4;
+  for (long k = long(blockIdx.x) * blockDim.x + threadIdx.x; k < n4; k += long(gridDim.x) * blockDim.x) {
+    const long i = a.shard_lo + 4 * k;
+    const float4 g = multimem_ld_add_v4(mc_grad + i);
+    float gv[4] = {g.x * a.grad_scale, g.y * a.grad_scale, g.z * a.grad_scale, g.w * a.grad_scale};
+    int gi = 0;
+    while (gi + 1 < a.ngroups && i >= a.groups[gi].hi) ++gi;
+    const DdpGroup& G = a.groups[gi];
+    const bool in_group = i >= G.lo && i < G.hi;
+    float4 pp = *reinterpret_cast<float4*>(a.master + i);
+    float* const mp = a.m + (i - a.mv_base);
+    float* const vp = a.v + (i - a.mv_base);
+    float4 mm = *reinterpret_cast<float4*>(mp);
+    float4 vv = *reinterpret_cast<float4*>(vp);
+    float* P = &pp.x;
+    float* M = &mm.x;
+    float* V = &vv.x;
+    if (in_group) {
+      const float decay = 1.f - G.lr * G.wd;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        ss += gv[j] * gv[j];
+        M[j] = M[j] * G.b1 + gv[j] * (1.f - G.b1);
+        V[j] = V[j] * G.b2 + gv[j] * gv[j] * (1.f - G.b2);
+        P[j] = P[j] * decay - ((M[j] * G.scale_m) / (sqrtf(V[j] * G.scale_v) + G.eps)) * G.lr;
+      }
+      *reinterpret_cast<float4*>(a.master + i) = pp;
+      *reinterpret_cast<float4*>(mp) = mm;
+      *reinterpret_cast<float4*>(vp) = vv;
+    }
+    multimem_st_v2(mc_work + i, make_uint2(pack_bf16x2(pp.x, pp.y), pack_bf16x2(pp.z, pp.w)));
+  }
+  fence_proxy_alias();
+  if (a.sumsq) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double t = 0;
+      for (int w = 0; w < int(blockDim.x / 32); ++w) t += red[w];
+      atomicAdd(a.sumsq, t);
+    }
+  }
+}
+
 void ddp_barrier(int64_t pads_dev, int64_t rank, int64_t world, int64_t epoch) {
   TORCH_CHECK(world >= 1 && world <= kMaxWorld && rank >= 0 && rank < world, "ddp_barrier: bad world");
   ddp_barrier_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
@@ -145,7 +225,8 @@ void ddp_barrier(int64_t pads_dev, int64_t rank, int64_t world, int64_t epoch) {
 // slice, or the whole buffer with mv_base 0).
 void ddp_rs_adam_ag(int64_t grads_dev, int64_t works_dev, int64_t world, torch::Tensor master, torch::Tensor m,
                     torch::Tensor v, int64_t shard_lo, int64_t shard_hi, torch::Tensor groups, double grad_scale,
-                    c10::optional<torch::Tensor> sumsq, int64_t mv_base) {
+                    c10::optional<torch::Tensor> sumsq, int64_t mv_base, int64_t mc_grad, int64_t mc_work,
+                    int64_t max_ctas) {
   TORCH_CHECK(world >= 1 && world <= kMaxWorld, "ddp: world size 1..8");
   TORCH_CHECK(master.scalar_type() == at::kFloat && m.scalar_type() == at::kFloat && v.scalar_type() == at::kFloat,
               "ddp: fp32 state");
@@ -184,7 +265,15 @@ void ddp_rs_adam_ag(int64_t grads_dev, int64_t works_dev, int64_t world, torch::
   const at::cuda::CUDAGuard guard(master.device());
   auto stream = at::cuda::getCurrentCUDAStream();
   const long n4 = (shard_hi - shard_lo) / 4;
-  const int blocks = int(std::max<long>(1, std::min<long>((n4 + 255) / 256, 148 * 8)));
+  const long cap = max_ctas > 0 ? max_ctas : 148 * 8;
+  const int blocks = int(std::max<long>(1, std::min<long>((n4 + 255) / 256, cap)));
+  if (mc_grad != 0 && mc_work != 0) {
+    TORCH_CHECK(mc_grad % 16 == 0 && mc_work % 16 == 0, "ddp: multicast addresses must be 16-byte aligned");
+    ddp_rs_adam_ag_nvls_kernel<<<blocks, 256, 0, stream>>>(a, reinterpret_cast<const float*>(mc_grad),
+                                                           reinterpret_cast<__nv_bfloat16*>(mc_work));
+    TORCH_CHECK(cudaGetLastError() == cudaSuccess, "ddp_rs_adam_ag (NVLS) launch failed");
+    return;
+  }
   switch (world) {
     case 1: ddp_rs_adam_ag_kernel<1><<<blocks, 256, 0, stream>>>(a); break;
     case 2: ddp_rs_adam_ag_kernel<2><<<blocks, 256, 0, stream>>>(a); break;

@@ -233,6 +233,114 @@ void softmax_xent(torch::Tensor logits, torch::Tensor targets, c10::optional<tor
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "softmax_xent launch failed");
 }
 
+// ---- cross-entropy from the lm_head GEMM's softmax partials ----------------------
+//
+// The lm_head GEMM (mode kLogitsStats) writes, next to the bf16 logits, the
+// (max, sum of 2^(v log2e - max)) of every row's 128-column groups. One CTA
+// per row combines the row's partials into the log-sum-exp (a 4 KB read for a
+// 65536 vocabulary instead of a pass over the 128 KB row), writes the NLL and,
+// for training, makes ONE pass over the row that replaces the logits by the
+// gradient (softmax - onehot) * scale. Against the two-pass softmax_xent this
+// saves one full read of the logits chunk.
+
+__device__ __forceinline__ void lse2_merge(float& m, float& s, float m2, float s2) {
+  const float mm = fmaxf(m, m2);
+  if (mm == -INFINITY) return;
+  s = (m == -INFINITY ? 0.f : s * ex2_approx(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * ex2_approx(m2 - mm));
+  m = mm;
+}
+
+__global__ void __launch_bounds__(kXentThreads, 4) xent_stats_kernel(
+    __nv_bfloat16* logits, long ld, const float2* __restrict__ stats, int G, const int64_t* __restrict__ targets,
+    float* __restrict__ nll_out, int V, float grad_scale, bool write_grad) {
+  __shared__ float red_m[kXentThreads / 32], red_s[kXentThreads / 32];
+  __shared__ float bc;
+  const int row = blockIdx.x;
+  __nv_bfloat16* lr = logits + long(row) * ld;
+  float m = -INFINITY, s = 0.f;
+  for (int g = threadIdx.x; g < G; g += kXentThreads) {
+    const float2 p = stats[long(row) * G + g];
+    lse2_merge(m, s, p.x, p.y);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    lse2_merge(m, s, m2, s2);
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  if (lane == 0) { red_m[warp] = m; red_s[warp] = s; }
+  __syncthreads();
+  if (warp == 0) {
+    m = lane < kXentThreads / 32 ? red_m[lane] : -INFINITY;
+    s = lane < kXentThreads / 32 ? red_s[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      lse2_merge(m, s, m2, s2);
+    }
+    if (lane == 0) bc = m + __log2f(s);
+  }
+  __syncthreads();
+  constexpr float kLn2 = 0.6931471805599453f, kLog2e = 1.4426950408889634f;
+  const float lse2 = bc;
+  const int64_t t = targets[row];
+  const bool valid = t >= 0 && t < V;
+  if (threadIdx.x == 0 && nll_out) nll_out[row] = valid ? lse2 * kLn2 - __bfloat162float(lr[t]) : 0.f;
+  if (!write_grad) return;
+  __syncthreads();  // lr[t] read above before it is overwritten
+  const float sc = valid ? grad_scale : 0.f;
+  constexpr int kStep = kXentThreads * 8;
+  auto grad8 = [&](uint4 w, int col0) {
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(ws[j]);
+      const int col = col0 + 2 * j;
+      const float g0 = ex2_approx(fmaf(f.x, kLog2e, -lse2)) - (col == t ? 1.f : 0.f);
+      const float g1 = ex2_approx(fmaf(f.y, kLog2e, -lse2)) - (col + 1 == t ? 1.f : 0.f);
+      o[j] = pack_bf16x2(g0 * sc, g1 * sc);
+    }
+    *reinterpret_cast<uint4*>(lr + col0) = make_uint4(o[0], o[1], o[2], o[3]);
+  };
+  int c = threadIdx.x * 8;
+  for (; c + 3 * kStep < V; c += 4 * kStep) {
+    uint4 w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) w[k] = *reinterpret_cast<const uint4*>(lr + c + k * kStep);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) grad8(w[k], c + k * kStep);
+  }
+  for (; c < V; c += kStep) grad8(*reinterpret_cast<const uint4*>(lr + c), c);
+}
+
+// logits: (rows, V) bf16 chunk written by gemm_logits_stats; stats: its
+// (rows, ceil(V / 128), 2) partials; targets: (rows,) int64, -1 = ignore.
+void xent_from_stats(torch::Tensor logits, torch::Tensor stats, torch::Tensor targets,
+                     c10::optional<torch::Tensor> nll, double grad_scale, bool write_grad) {
+  TORCH_CHECK(logits.scalar_type() == at::kBFloat16 && logits.dim() == 2 && logits.stride(1) == 1, "xent: logits");
+  TORCH_CHECK(targets.scalar_type() == at::kLong && targets.is_contiguous(), "xent: int64 targets");
+  const int rows = int(logits.size(0)), V = int(logits.size(1));
+  const int G = (V + 127) / 128;
+  TORCH_CHECK(targets.numel() == rows, "xent: targets length");
+  TORCH_CHECK(V % 8 == 0 && logits.stride(0) % 8 == 0, "xent: V and row stride must be multiples of 8");
+  TORCH_CHECK(stats.scalar_type() == at::kFloat && stats.is_contiguous() && stats.dim() == 3 && stats.size(0) >= rows &&
+                  stats.size(1) == G && stats.size(2) == 2,
+              "xent: stats must be (rows, ceil(V / 128), 2) fp32");
+  float* np = nullptr;
+  if (nll.has_value()) {
+    TORCH_CHECK(nll->scalar_type() == at::kFloat && nll->numel() == rows, "xent: nll");
+    np = nll->data_ptr<float>();
+  }
+  const at::cuda::CUDAGuard guard(logits.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  xent_stats_kernel<<<rows, kXentThreads, 0, stream>>>(
+      reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), logits.stride(0),
+      reinterpret_cast<const float2*>(stats.data_ptr<float>()), G, targets.data_ptr<int64_t>(), np, V,
+      float(grad_scale), write_grad);
+  TORCH_CHECK(cudaGetLastError() == cudaSuccess, "xent_from_stats launch failed");
+}
+
 // ---- AdamW -----------------------------------------------------------------------
 
 struct AdamParams {

@@ -39,6 +39,7 @@ enum GemmMode : int {
   kRopeNorm = 5,    // QKV projection: q and k heads get RoPE + RMSNorm over head_dim, v stored plain
   kAtomicF32T = 6,  // C^T(fp32) += alpha*acc: C is [N, M]; a warp's 32 rows hit 32 adjacent floats
   kDRelu2Act = 7,   // C = alpha*acc * 2*sqrt(AUX), AUX = relu(h)^2 (the ReLU^2 output)
+  kLogitsStats = 8, // C = alpha*acc (bf16 logits) + per (row, 128-column group) softmax partials
 };
 
 struct GemmArgs {
@@ -67,6 +68,10 @@ struct GemmArgs {
   // dependent launch its first tiles are fetched before griddepcontrol.wait.
   int a_independent;
   int rotate;  // single-output epilogues rotate through all staging buffers
+  // kLogitsStats: (max, sum of exp(v - max)) over the bf16-rounded logits of
+  // row r, columns [128 g, 128 g + 128), at stats[r * stats_ld + g].
+  float2* stats;
+  int stats_ld;
 };
 
 constexpr int BM = 128, BK = 64, kGroupM = 16;
@@ -245,7 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // extent (TMA fills zeros); the debug build checks that a box starts no
       // further out than one tile.
       auto load = [&](void* dst, const CUtensorMap* map, int stage_, int c0, int c1, int n0, int n1) {
-        if (!NK_IN_BOUNDS(c0 % 8 == 0 && c0 >= 0 && c1 >= 0 && c0 < n0 + BK && c1 < n1 + 2 * BM, args.err)) return;
+        if (!NK_IN_BOUNDS(c0 % 8 == 0 && c0 >= 0 && c1 >= 0 && c0 < n0 + 2 * BM && c1 < n1 + 2 * BM, args.err)) return;
         if (PAIR) tma_load_2d_pair(dst, map, map_to_cta(&full_bar[stage_], 0), c0, c1);
         else tma_load_2d(dst, map, &full_bar[stage_], c0, c1);
       };
@@ -423,6 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int c_begin = half * (BN / 64), c_end = (half + 1) * (BN / 64);
       if (need_aux && n * BN + c_begin * 32 < args.N) issue_aux(ck, n * BN + c_begin * 32, row0);
+      float st_m = -INFINITY, st_s = 0.f;  // kLogitsStats running partials (log2 domain)
 #pragma unroll 1
       for (int c = c_begin; c < c_end; ++c) {
         const int col0 = n * BN + c * 32;
@@ -467,6 +473,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           else bulk_wait_read<NB / 2 - 1>();
         }
         __syncwarp();
+        if (args.mode == kLogitsStats) {
+          // Softmax partials of the values as stored (bf16), in log2 units:
+          // m = max(v) * log2e, s = sum 2^(v * log2e - m).
+          constexpr float kLog2e = 1.4426950408889634f;
+          float cm = -INFINITY;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            x[i] = __bfloat162float(__float2bfloat16(x[i]));
+            if (col0 + i < args.N) cm = fmaxf(cm, x[i] * kLog2e);
+          }
+          if (cm > st_m) {
+            st_s *= ex2_approx(st_m - cm);  // st_m = -inf at first: st_s is 0 and stays 0
+            st_m = cm;
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (col0 + i < args.N) st_s += ex2_approx(fmaf(x[i], kLog2e, -st_m));
+        }
         if (args.mode == kRelu2) {
           if (keep_h) stage_row_store(bufX(ck), lane, x);  // pre-activation h
 #pragma unroll
@@ -488,6 +512,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           bulk_commit();
         }
         ++ck;
+      }
+      if (args.mode == kLogitsStats && ok) {
+        const int row = row0 + lane, g = (n * BN + half * 128) / 128;
+        if (row < args.M && n * BN + half * 128 < args.N) args.stats[long(row) * args.stats_ld + g] = make_float2(st_m, st_s);
       }
       tc_fence_before();
       __syncwarp();
@@ -615,7 +643,10 @@ void gemm_impl(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_majo
   args.err = error_word();
   args.a_independent = a_independent ? 1 : 0;
   args.rotate = rotate_mode();
-  if (rope) {
+  if (rope && mode == kLogitsStats) {
+    args.stats = rope->stats;
+    args.stats_ld = rope->stats_ld;
+  } else if (rope) {
     args.rope_cos = rope->rope_cos; args.rope_sin = rope->rope_sin; args.rope_rstd = rope->rope_rstd;
     args.rope_T = rope->rope_T; args.rope_ld = rope->rope_ld; args.rope_H = rope->rope_H; args.rope_C = rope->rope_C; args.rope_eps = rope->rope_eps;
   }
@@ -674,6 +705,20 @@ void gemm(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_major, to
   TORCH_CHECK(mode != kRopeNorm, "gemm: use gemm_qkv_rope for the RoPE epilogue");
   TORCH_CHECK(mode >= kStoreBf16 && mode <= kDRelu2Act, "gemm: unknown epilogue mode");
   gemm_impl(A, a_mn_major, B, b_mn_major, C, mode, alpha, aux, aux_out, splits, block_n, nullptr);
+}
+
+// logits[M, V] = x[M, K] . w[V, K]^T (bf16) with the softmax partials of each
+// row's 128-column groups in stats (M, ceil(V / 128), 2) fp32: the lm_head of
+// the fused loss head (the log-sum-exp then needs no pass over the logits).
+void gemm_logits_stats(torch::Tensor x, torch::Tensor w, torch::Tensor logits, torch::Tensor stats) {
+  const int64_t M = x.size(0), V = w.size(0);
+  TORCH_CHECK(stats.scalar_type() == at::kFloat && stats.is_contiguous() && stats.dim() == 3 && stats.size(0) >= M &&
+                  stats.size(1) == (V + 127) / 128 && stats.size(2) == 2,
+              "gemm_logits_stats: stats must be (rows, ceil(V / 128), 2) fp32");
+  GemmArgs r{};
+  r.stats = reinterpret_cast<float2*>(stats.data_ptr<float>());
+  r.stats_ld = int(stats.size(1));
+  gemm_impl(x, false, w, false, logits, kLogitsStats, 1.0, c10::nullopt, c10::nullopt, 1, 256, &r);
 }
 
 // qkv[M, 3C] = x[M, C] . w[3C, C]^T with RoPE + QK-RMSNorm fused into the

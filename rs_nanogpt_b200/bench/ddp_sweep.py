@@ -14,6 +14,9 @@ For each bucket of S MB of fp32 gradients, on every rank:
                 AdamW kernel over the whole bucket on every rank.
 * ``nccl_rsag`` ZeRO-1 baseline: NCCL reduce-scatter, AdamW on the shard,
                 NCCL all-gather of the bf16 shard.
+* ``fused_nvls`` the same fused step through NVLink SHARP (multimem.ld_reduce
+                of the shard's gradient sum, multimem.st of the bf16 weights to
+                every rank), when the switch offers multicast.
 
 Times are CUDA events per step, max over ranks. For a bucket of n fp32
 elements one rank of the fused step reads 4·(W-1)·n/W bytes of peer gradients
@@ -64,6 +67,18 @@ def main(argv=None):
     torch.cuda.synchronize()
     td.barrier()
     hg, hw, hp = (symm.rendezvous(t, group.group_name) for t in (grad, work, pads))
+
+    def multicast(h, t):
+        try:
+            hm = h.has_multicast_support
+            base = int(h.multicast_ptr) if (hm() if callable(hm) else hm) else 0
+        except (AttributeError, RuntimeError):
+            base = 0
+        return base + (t.data_ptr() - int(h.buffer_ptrs[rank])) if base else 0
+
+    mc = (multicast(hg, grad), multicast(hw, work))
+    if not (mc[0] and mc[1]):
+        mc = (0, 0)
     master = torch.randn(nmax, device=dev)
     m = torch.zeros(nmax, device=dev)
     v = torch.zeros(nmax, device=dev)
@@ -96,10 +111,10 @@ def main(argv=None):
         lo, hi = min(n, rank * shard), min(n, rank * shard + shard)
         groups = torch.tensor([[0, n, 1e-4, 0.9, 0.95, 1e-8, 0.1, 10.0, 20.0]], dtype=torch.float64)
 
-        def fused():
+        def fused(mc=(0, 0)):
             barrier()
             ext().ddp_rs_adam_ag(int(hg.buffer_ptrs_dev), int(hw.buffer_ptrs_dev), world, master, m, v, lo, hi,
-                                 groups, 1.0 / world, None, 0)
+                                 groups, 1.0 / world, None, 0, mc[0], mc[1])
             barrier()
 
         g_ar = torch.randn(n, device=dev)
@@ -122,12 +137,17 @@ def main(argv=None):
             td.all_gather_into_tensor(w_full, w_shard)
 
         t_f, t_ar, t_rs = timed(fused), timed(nccl_ar), timed(nccl_rsag)
+        t_nv = timed(lambda: fused(mc)) if mc[0] else None
         bytes_in = 4.0 * (world - 1) * shard
         bytes_out = 2.0 * (world - 1) * shard
         roof = max(bytes_in, bytes_out) / (LINK_GBS * 1e9) * 1e3
         rows.append({"bucket_mb": mb, "fused_ms": t_f, "nccl_ar_ms": t_ar, "nccl_rsag_ms": t_rs,
                      "roofline_ms": roof, "fused_frac": roof / t_f if world > 1 else None,
-                     "speedup_vs_nccl_ar": t_ar / t_f})
+                     "speedup_vs_nccl_ar": t_ar / t_f, "fused_nvls_ms": t_nv,
+                     # NVLS: each GPU still sends its gradient of every other rank's shard to the switch
+                     # once (out: 4(W-1) + 2 bytes per shard element; in: 4 + 2(W-1)).
+                     "nvls_roofline_ms": max(4.0 * (world - 1) + 2.0, 4.0 + 2.0 * (world - 1)) * shard
+                     / (LINK_GBS * 1e9) * 1e3})
         del g_ar, w_ar, g_full, g_shard, w_shard, w_full
         if rank == 0:
             print(json.dumps(rows[-1]), flush=True)

@@ -12,9 +12,11 @@ Per block (rs-nanogpt src/model/block.rs:49-60 semantics):
     a,hp = relu(h2 Wfc^T)^2, h2 Wfc^T              GEMM, ReLU^2 epilogue (keeps hp)
     x''  = x' + a Wmlp^T                           GEMM, residual-add epilogue
 
-The loss head runs chunk by chunk over the token rows: logits = rms(x_L) Wlm^T,
-then one kernel computes the fp32 log-sum-exp, the per-row NLL and, for
-training, the logits gradient in place; the lm_head data and weight gradients
+The loss head runs chunk by chunk over the token rows: logits = rms(x_L) Wlm^T
+from a GEMM whose epilogue also writes every row's softmax partials (max and
+sum of exponentials per 128 columns), then one kernel combines them into the
+log-sum-exp, writes the per-row NLL and, for training, overwrites the logits
+with their gradient in a single pass; the lm_head data and weight gradients
 follow immediately, so the (B*T, V) logits never exist in memory at once.
 Because the loss is the last op, the lm_head backward is done during the
 forward pass.
@@ -67,6 +69,7 @@ class _Workspace:
         self.nll = torch.empty(m, **f32)
         rows = max(1, min(m, XENT_CHUNK_BYTES // (2 * cfg.vocab_size)))
         self.logits = torch.empty(rows, cfg.vocab_size, **bf)
+        self.xstats = torch.empty(rows, (cfg.vocab_size + 127) // 128, 2, **f32)  # lm_head softmax partials
         if train:
             self.dhf = torch.empty(m, c, **bf)
             self.dx = torch.empty(m, c, **bf)
@@ -96,6 +99,9 @@ class FusedGpt:
         # RoPE + QK-norm live in the QKV GEMM epilogue (forward) and in the
         # attention backward's dQ/dK write-out when the shapes allow it.
         self.fuse_rope = gemm.qkv_rope_supported(self.cfg.n_embd, self.cfg.head_dim)
+        # Loss head: softmax partials from the lm_head GEMM epilogue + a one-pass
+        # loss/gradient kernel (NANOGPT_XENT_STATS=0: the two-pass softmax_xent).
+        self.xent_stats = os.environ.get("NANOGPT_XENT_STATS", "1") == "1"
 
     def _side_stream(self) -> torch.cuda.Stream:
         if getattr(self, "_side", None) is None:
@@ -149,9 +155,15 @@ class FusedGpt:
         for r0 in range(0, m, rows):
             r1 = min(m, r0 + rows)
             logits = ws.logits[: r1 - r0]
-            gemm.linear(hf[r0:r1], w, out=logits)
             train = grad_scale is not None
-            L.softmax_xent(logits, tg[r0:r1], ws.nll[r0:r1], grad_scale or 0.0, train)
+            if self.xent_stats:
+                # The GEMM epilogue also writes each row's softmax partials, so
+                # the loss needs one pass over the chunk (gradient in place).
+                gemm.linear_logits_stats(hf[r0:r1], w, logits, ws.xstats[: r1 - r0])
+                L.xent_from_stats(logits, ws.xstats[: r1 - r0], tg[r0:r1], ws.nll[r0:r1], grad_scale or 0.0, train)
+            else:
+                gemm.linear(hf[r0:r1], w, out=logits)
+                L.softmax_xent(logits, tg[r0:r1], ws.nll[r0:r1], grad_scale or 0.0, train)
             if train:
                 gemm.linear_dgrad(logits, w, out=ws.dhf[r0:r1])
                 gemm.linear_wgrad(logits, hf[r0:r1], st.grad_of("lm_head.weight"))

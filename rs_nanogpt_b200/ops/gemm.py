@@ -37,6 +37,14 @@ def linear(x, w, out=None, alpha: float = 1.0):
     return out
 
 
+def linear_logits_stats(x, w, out, stats):
+    """out[M,V] = x[M,K] @ w[V,K]^T (bf16) and, per row and 128-column group,
+    the softmax partials (max, sum 2^(v log2e - max)) of the stored logits in
+    ``stats`` (M, ceil(V / 128), 2) fp32 -- the fused loss head's lm_head."""
+    ext().gemm_logits_stats(x, w, out, stats)
+    return out
+
+
 def linear_relu2(x, w, act=None, h=None):
     """(act, h): h = x w^T and act = relu(h)^2, both bf16, in one GEMM."""
     m, n = x.shape[0], w.shape[0]

@@ -52,6 +52,15 @@ def softmax_xent(logits, targets, nll: Optional[torch.Tensor] = None, grad_scale
     ext().softmax_xent(logits, targets, nll, grad_scale, write_grad)
 
 
+def xent_from_stats(logits, stats, targets, nll: Optional[torch.Tensor] = None, grad_scale: float = 0.0,
+                    write_grad: bool = False) -> None:
+    """Cross-entropy of a logits chunk written by ``gemm.linear_logits_stats``:
+    the per-row log-sum-exp comes from the GEMM's softmax partials ``stats``;
+    writes the NLL and, with ``write_grad``, (softmax - onehot) * grad_scale
+    over the logits in place in one pass."""
+    ext().xent_from_stats(logits, stats, targets, nll, grad_scale, write_grad)
+
+
 def adamw(p, g, m, v, work, lr, b1, b2, eps, wd, step, grad_scale=1.0) -> None:
     ext().adamw_step(p, g, m, v, work, lr, b1, b2, eps, wd, step, grad_scale)
 

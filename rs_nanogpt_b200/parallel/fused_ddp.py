@@ -22,6 +22,7 @@ rebuilds the full master when a checkpoint or a sample needs it.
 ``gather_optimizer`` / ``load_optimizer`` convert the sharded moments to and
 from the full flat layout of a checkpoint's ``optim.pt``.
 """
+import os
 from typing import Optional
 
 import torch
@@ -62,6 +63,17 @@ class FusedDdp:
         self.h_work = symm.rendezvous(work, name)
         self.h_pads = symm.rendezvous(pads, name)
         store.grad, store.work = grad, work
+        # NVLink SHARP (NANOGPT_DDP_NVLS=1, when the switch supports it):
+        # multicast addresses of the gradient and working-copy buffers. Off by
+        # default: the per-peer path is the measured one.
+        self.mc_grad = self.mc_work = 0
+        if os.environ.get("NANOGPT_DDP_NVLS", "0") == "1":
+            self.mc_grad = self._multicast(self.h_grad, grad)
+            self.mc_work = self._multicast(self.h_work, work)
+            if not (self.mc_grad and self.mc_work):
+                self.mc_grad = self.mc_work = 0
+        # CTAs of the step kernel (it shares the SMs with the backward it overlaps).
+        self.max_ctas = int(os.environ.get("NANOGPT_DDP_CTAS", "0"))
         self._keep = (grad, work, pads)
         self.epoch = 0
         self.sumsq = torch.zeros(1, dtype=torch.float64, device=dev)
@@ -96,6 +108,22 @@ class FusedDdp:
         self._groups_t = None
         self._grad_scale = 1.0
 
+    def _multicast(self, handle, t: torch.Tensor) -> int:
+        try:
+            hm = handle.has_multicast_support
+            if not (hm() if callable(hm) else hm):
+                return 0
+            base = int(handle.multicast_ptr)
+        except (AttributeError, RuntimeError):
+            return 0
+        if base == 0:
+            return 0
+        return base + (t.data_ptr() - int(handle.buffer_ptrs[self.rank]))
+
+    @property
+    def nvls(self) -> bool:
+        return self.mc_grad != 0
+
     def _barrier(self) -> None:
         self.epoch += 1
         ext().ddp_barrier(int(self.h_pads.buffer_ptrs_dev), self.rank, self.world, self.epoch)
@@ -117,7 +145,8 @@ class FusedDdp:
             o = self.mv_off[key]
             ext().ddp_rs_adam_ag(int(self.h_grad.buffer_ptrs_dev), int(self.h_work.buffer_ptrs_dev), self.world,
                                  self.store.master, self.m[o:o + sh], self.v[o:o + sh], lo, hi, self._groups_t,
-                                 self._grad_scale / self.world, self.sumsq, lo)
+                                 self._grad_scale / self.world, self.sumsq, lo, self.mc_grad, self.mc_work,
+                                 self.max_ctas)
 
     # -- one optimizer step ---------------------------------------------------------
 

@@ -64,8 +64,8 @@ for ignored in (False, True):
     a, b = engines["nccl"].store, engines["fused"].store
     diff = (a.master - b.master).abs().max().item()
     wdiff = (a.work.float() - b.work.float()).abs().max().item()
-    print(f"rank {dist.rank()} ignored={ignored} master diff {diff:.3e} work diff {wdiff:.3e} norms {norms}",
-          flush=True)
+    print(f"rank {dist.rank()} ignored={ignored} nvls={engines['fused'].fused_ddp.nvls} master diff {diff:.3e} "
+          f"work diff {wdiff:.3e} norms {norms}", flush=True)
     assert kernel_status() == 0
     assert diff < 1e-5, diff
     assert wdiff < 1e-2, wdiff
@@ -107,11 +107,14 @@ def _gpus():
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_fused_ddp_matches_nccl_baseline(tmp_path, world):
+@pytest.mark.parametrize("nvls", ["0", "1"])
+def test_fused_ddp_matches_nccl_baseline(tmp_path, world, nvls):
+    """nvls=1 runs the NVLink SHARP kernel (multimem) where the switch offers
+    multicast; elsewhere that case checks the per-peer fallback again."""
     if _gpus() < world:
         pytest.skip(f"needs {world} GPUs")
     from rs_nanogpt_b200.parallel.launcher import spawn_ranks, supervise_ranks
     script = tmp_path / "ddp.py"
     script.write_text(SCRIPT)
-    env = {"PYTHONPATH": ROOT + os.pathsep + os.environ.get("PYTHONPATH", "")}
+    env = {"PYTHONPATH": ROOT + os.pathsep + os.environ.get("PYTHONPATH", ""), "NANOGPT_DDP_NVLS": nvls}
     assert supervise_ranks(spawn_ranks(world, [sys.executable, str(script)], env)) == 0

@@ -108,6 +108,32 @@ def test_softmax_xent():
         _close(logits, lf.grad, 1e-2)
 
 
+@pytest.mark.parametrize("rows,v,k", [(300, 65536, 256), (129, 1000, 136), (64, 32776, 64)])
+def test_fused_lm_head_cross_entropy(rows, v, k):
+    """lm_head GEMM with the softmax-partials epilogue + the one-pass loss /
+    gradient kernel vs fp32 autograd of the reference masked NLL on the same
+    bf16 logits (ignore_index -1 rows included, ragged vocabularies)."""
+    from rs_nanogpt_b200.models.reference import masked_nll
+    from rs_nanogpt_b200.ops import gemm
+    from rs_nanogpt_b200.ops import layers as L
+    torch.manual_seed(13)
+    x = torch.randn(rows, k, device="cuda").bfloat16()
+    w = (torch.randn(v, k, device="cuda") * 0.2).bfloat16()
+    tg = torch.randint(0, v, (rows,), device="cuda")
+    tg[::7] = -1
+    logits = torch.empty(rows, v, device="cuda", dtype=torch.bfloat16)
+    stats = torch.empty(rows, (v + 127) // 128, 2, device="cuda")
+    gemm.linear_logits_stats(x, w, logits, stats)
+    _close(logits, x.float() @ w.float().t(), 2e-2)
+    lf = logits.float().requires_grad_(True)
+    nll_ref, _ = masked_nll(lf, tg)
+    (nll_ref.sum() * 0.5).backward()
+    nll = torch.empty(rows, device="cuda")
+    L.xent_from_stats(logits, stats, tg, nll, 0.5, True)
+    _close(nll, nll_ref, 1e-3)
+    _close(logits, lf.grad, 1e-2)
+
+
 def test_embedding_fwd_bwd():
     from rs_nanogpt_b200.ops import layers as L
     torch.manual_seed(4)
