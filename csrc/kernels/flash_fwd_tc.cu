@@ -11,8 +11,10 @@
 //   warps 2-5   softmax for tile 0, warps 6-9 for tile 1: thread = query row.
 //               Reads its S row from TMEM, applies the causal mask on the
 //               diagonal block, keeps the running max / sum in registers,
-//               writes P (bf16) to shared memory in the UMMA K-major swizzled
-//               layout, and rescales its O row in TMEM only when the row max
+//               writes P (bf16 pairs) back to tensor memory over the S
+//               columns it has read (the P V MMA takes its A operand from
+//               tensor memory; NANOGPT_FWD_P_TMEM=0 stages P in shared memory
+//               instead), and rescales its O row in TMEM only when the row max
 //               grew by more than 2^8 since the last rescale (otherwise the
 //               stale max is kept, which only scales P and O by the same
 //               bounded factor).
@@ -21,6 +23,8 @@
 //
 // Output and LSE conventions match flash_attn.cu (LSE in base-2 units of the
 // scaled scores), so the backward kernels consume either forward's results.
+#include <cstdlib>
+
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -55,6 +59,7 @@ __device__ __forceinline__ uint32_t p_off(int r, int c) {
   return uint32_t((c >> 3) * fa::kSubBytes + r * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
 
+template <bool P_TMEM>
 __global__ void __launch_bounds__(fa::kThreads, 1)
     flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm, const FaArgs a) {
   using namespace fa;
@@ -145,9 +150,15 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
         const uint32_t p = smem_u32(sP + t * kTileBytes), v = smem_u32(sV);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint32_t poff = (kk >> 2) * kSubBytes + (kk & 3) * 32;
-          umma_bf16(tmem + 256 + t * HD, sw128_desc(p + poff, 16, 1024), sw128_desc(v + kk * 2048, kSubBytes, 1024),
-                    id_o, (j > 0 || kk > 0) ? 1u : 0u);
+          if constexpr (P_TMEM) {
+            // P_t packed as bf16 pairs in TMEM columns [t * BN, t * BN + 64): keys 16 kk.. in 8 columns.
+            umma_bf16_ts(tmem + 256 + t * HD, tmem + t * BN + 8 * kk, sw128_desc(v + kk * 2048, kSubBytes, 1024),
+                         id_o, (j > 0 || kk > 0) ? 1u : 0u);
+          } else {
+            const uint32_t poff = (kk >> 2) * kSubBytes + (kk & 3) * 32;
+            umma_bf16(tmem + 256 + t * HD, sw128_desc(p + poff, 16, 1024),
+                      sw128_desc(v + kk * 2048, kSubBytes, 1024), id_o, (j > 0 || kk > 0) ? 1u : 0u);
+          }
         }
         umma_commit(&o_done[t]);
       };
@@ -238,15 +249,20 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const float p0 = exp2f(fmaf(sv[c * 32 + i], a.sl2, -m_used));
-          const float p1 = exp2f(fmaf(sv[c * 32 + i + 1], a.sl2, -m_used));
+          const float p0 = ex2_approx(fmaf(sv[c * 32 + i], a.sl2, -m_used));
+          const float p1 = ex2_approx(fmaf(sv[c * 32 + i + 1], a.sl2, -m_used));
           rs += p0 + p1;
           pk[i / 2] = pack_bf16x2(p0, p1);
         }
+        if constexpr (P_TMEM) {
+          // Over this row's own S columns, all of which are already in registers.
+          tmem_st_32x16(t_s + 16 * c, pk);
+        } else {
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          *reinterpret_cast<uint4*>(P + p_off(r, c * 4 + q)) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2],
-                                                                           pk[4 * q + 3]);
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(P + p_off(r, c * 4 + q)) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2],
+                                                                             pk[4 * q + 3]);
+        }
       }
       l += rs;
       fence_proxy_async();  // generic-proxy smem writes -> visible to the tensor core
@@ -309,15 +325,22 @@ void flash_fwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor lse, int64
   a.B = int(B); a.H = int(H); a.T = int(T); a.C = int(C);
   a.sl2 = (1.f / std::sqrt(float(HD))) * 1.4426950408889634f;
   a.err = error_word();
+  static const int p_tmem = [] {
+    const char* e = std::getenv("NANOGPT_FWD_P_TMEM");
+    return e ? std::atoi(e) : 1;
+  }();
   static bool configured = false;
   if (!configured) {
-    TORCH_CHECK(cudaFuncSetAttribute(flash_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) ==
+    TORCH_CHECK(cudaFuncSetAttribute(flash_fwd_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) ==
+                    cudaSuccess && cudaFuncSetAttribute(flash_fwd_tc_kernel<false>,
+                                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) ==
                     cudaSuccess, "flash_tc: smem");
     configured = true;
   }
   const at::cuda::CUDAGuard guard(qkv.device());
   dim3 grid(unsigned(T / 256), unsigned(B * H));
-  flash_fwd_tc_kernel<<<grid, kThreads, kSmem, at::cuda::getCurrentCUDAStream()>>>(m, a);
+  if (p_tmem) flash_fwd_tc_kernel<true><<<grid, kThreads, kSmem, at::cuda::getCurrentCUDAStream()>>>(m, a);
+  else flash_fwd_tc_kernel<false><<<grid, kThreads, kSmem, at::cuda::getCurrentCUDAStream()>>>(m, a);
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "flash_fwd_tc launch failed");
 }
 
