@@ -70,8 +70,7 @@ def main(argv=None):
 
     def multicast(h, t):
         try:
-            hm = h.has_multicast_support
-            base = int(h.multicast_ptr) if (hm() if callable(hm) else hm) else 0
+            base = int(h.multicast_ptr)  # 0 when the switch offers no multicast
         except (AttributeError, RuntimeError):
             base = 0
         return base + (t.data_ptr() - int(h.buffer_ptrs[rank])) if base else 0

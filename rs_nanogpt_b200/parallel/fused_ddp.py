@@ -110,10 +110,7 @@ class FusedDdp:
 
     def _multicast(self, handle, t: torch.Tensor) -> int:
         try:
-            hm = handle.has_multicast_support
-            if not (hm() if callable(hm) else hm):
-                return 0
-            base = int(handle.multicast_ptr)
+            base = int(handle.multicast_ptr)  # 0 when the switch offers no multicast
         except (AttributeError, RuntimeError):
             return 0
         if base == 0:
