@@ -25,7 +25,14 @@ def _sms() -> int:
     return _NUM_SMS
 
 
+# Output widths up to this many columns use 128-column tiles (measurement
+# switch NANOGPT_GEMM_BN128_MAX_N; 0 = 256-column tiles wherever they divide N).
+_BN128_MAX_N = int(os.environ.get("NANOGPT_GEMM_BN128_MAX_N", "0"))
+
+
 def _block_n(n: int) -> int:
+    if n <= _BN128_MAX_N:
+        return 128
     return 256 if n >= 256 and n % 256 == 0 else 128
 
 
