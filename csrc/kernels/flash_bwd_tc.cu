@@ -83,7 +83,8 @@ struct FbArgs {
   // bit 5 makes the MMA warp skip its wait for the dQ^T drain, bit 7 loads only
   // the first stages' Q / dO (later stages are released without a copy), bit 8
   // skips the dK / dV write-out, bit 9 records a timeline (g_fb_trace), bit 13
-  // adds dQ with red.global.add from registers instead of TMA reduce-adds.
+  // adds dQ with red.global.add from registers instead of TMA reduce-adds, bit 14
+  // makes the MMA warp skip its wait for the softmax warps.
   int dbg;
 };
 
@@ -225,7 +226,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
         const int st = n % NS, u = n & 1;
         if (n + 1 < nblk && !scores(n + 1)) break;
         fb_stamp(a, n, 0);
-        if (!mbar_wait(&p_full[u], (n >> 1) & 1, kErrTimeoutMma, a.err)) break;
+        if (!(a.dbg & 16384) && !mbar_wait(&p_full[u], (n >> 1) & 1, kErrTimeoutMma, a.err)) break;
         fb_stamp(a, n, 1);
         tc_fence_after();
         const uint32_t q = smem_u32(sQ + st * kQTile), o = smem_u32(sO + st * kQTile);
