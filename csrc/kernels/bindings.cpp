@@ -57,6 +57,7 @@ void qkv_decode_finish(torch::Tensor acc, torch::Tensor qkv, torch::Tensor k_cac
                        torch::Tensor pos, torch::Tensor cos_t, torch::Tensor sin_t, int64_t H, double eps);
 void gemm_skinny_acc(torch::Tensor w, torch::Tensor x, torch::Tensor acc, int64_t splits);
 void set_pdl(bool on);
+torch::Tensor gemm_trace();
 }  // namespace nk
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -99,5 +100,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("skinny_finish", &nk::skinny_finish);
   m.def("qkv_decode_finish", &nk::qkv_decode_finish);
   m.def("gemm_skinny_acc", &nk::gemm_skinny_acc);
+  m.def("gemm_trace", &nk::gemm_trace, "MMA-warp wait accounting of the last traced GEMM (measurement)");
   m.def("set_pdl", &nk::set_pdl, "programmatic dependent launch for the decode-chain kernels");
 }

@@ -72,7 +72,13 @@ struct GemmArgs {
   // row r, columns [128 g, 128 g + 128), at stats[r * stats_ld + g].
   float2* stats;
   int stats_ld;
+  int trace;  // NANOGPT_GEMM_TRACE: account the MMA warp's waits in g_gemm_trace
 };
+
+// Measurement (NANOGPT_GEMM_TRACE=1): per CTA, the MMA warp's cycles waiting
+// for a free accumulator (epilogue behind), waiting for operands (loads
+// behind), its total cycles, and its tiles. Read with gemm_trace().
+__device__ long long g_gemm_trace[1024 * 4];
 
 constexpr int BM = 128, BK = 64, kGroupM = 16;
 constexpr int kEpiWarps = 8, kThreads = 64 + 32 * kEpiWarps;
@@ -298,16 +304,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_commit(bar);
         }
       };
+      long long w_acc = 0, w_ld = 0;
+      const long long t_begin = clock64();
       for (int u = cta_id; u < units && ok; u += n_ctas, ++local) {
         int m, n, kb0, kb1;
         unit_coords(args, u, m, n, kb0, kb1);
         const int b = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
+        long long t0 = args.trace ? clock64() : 0;
         if (!mbar_wait(&acc_empty[b], acc_phase ^ 1, kErrTimeoutMma, args.err)) break;
+        if (args.trace) w_acc += clock64() - t0;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + b * BN;
         for (int kb = kb0; kb < kb1; ++kb) {
+          if (args.trace) t0 = clock64();
           if (!mbar_wait(&full_bar[stage], phase, kErrTimeoutMma, args.err)) { ok = false; break; }
+          if (args.trace) w_ld += clock64() - t0;
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * S::kStageBytes);
           const uint32_t sb = sa + S::kABytes;
@@ -324,6 +336,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
         commit(&acc_full[b]);
+      }
+      if (args.trace && blockIdx.x < 1024) {
+        long long* t = g_gemm_trace + blockIdx.x * 4;
+        t[0] = w_acc; t[1] = w_ld; t[2] = clock64() - t_begin; t[3] = local;
       }
     }
   } else {
@@ -582,6 +598,13 @@ static void launch(const GemmArgs& args, const CUtensorMap& ta, const CUtensorMa
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "gemm launch failed");
 }
 
+torch::Tensor gemm_trace() {
+  auto out = torch::zeros({1024, 4}, torch::dtype(torch::kInt64));
+  TORCH_CHECK(cudaMemcpyFromSymbol(out.data_ptr(), g_gemm_trace, sizeof(long long) * 1024 * 4) == cudaSuccess,
+              "gemm_trace: copy failed");
+  return out;
+}
+
 // CTA pairs (cta_group::2) for the large 256-column GEMMs. NANOGPT_GEMM_PAIR:
 // unset/1 = where measured faster (below), 0 = never, 2 = for every eligible
 // product (measurement switch).
@@ -643,6 +666,11 @@ void gemm_impl(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_majo
   args.err = error_word();
   args.a_independent = a_independent ? 1 : 0;
   args.rotate = rotate_mode();
+  static const int trace = [] {
+    const char* e = std::getenv("NANOGPT_GEMM_TRACE");
+    return e ? std::atoi(e) : 0;
+  }();
+  args.trace = trace;
   if (rope && mode == kLogitsStats) {
     args.stats = rope->stats;
     args.stats_ld = rope->stats_ld;

@@ -14,7 +14,7 @@ import functools
 # call's arguments).
 _LAUNCHES = {"flash_bwd": 3, "flash_bwd_tc": lambda *a, **k: 2 if (a[-1] is True or k.get("prepared")) else 3,
              "flash_bwd_prep": 1, "kernel_status": 0, "flash_fwd_tc_supported": 0,
-             "flash_bwd_tc_supported": 0, "flash_bwd_trace": 0, "set_pdl": 0,
+             "flash_bwd_tc_supported": 0, "flash_bwd_trace": 0, "gemm_trace": 0, "set_pdl": 0,
              "decode_attention": lambda qkv, kc, vc, pos, out, po, pm, chunk: 1 + int(kc.shape[2] > chunk)}
 _count = [0]
 
