@@ -571,15 +571,59 @@ void flash_dsum(torch::Tensor out, torch::Tensor dout, torch::Tensor dsum, int64
 // The backward's memory-bound preparation: D = rowsum(dO o O) and the zeroed
 // fp32 dQ accumulator. Separate so a caller can run it on another stream
 // (next to an independent GEMM) and then call flash_bwd_tc with prepared=true.
+// The backward's preparation in one memory pass: D = rowsum(dO o O) per
+// (token, head) and the zeroed fp32 dQ accumulator. Half a warp per (token,
+// head): each lane reads 8 bf16 of O and of dO (16-byte loads), the 16 lanes
+// reduce with shuffles, and each lane clears 8 floats of the head's dQ row.
+__global__ void __launch_bounds__(256) flash_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, long ld_o,
+                                                             const __nv_bfloat16* __restrict__ dout, long ld_do,
+                                                             float* __restrict__ dsum, float* __restrict__ dq_acc,
+                                                             long items, int T, int H, int C) {
+  const long item = (long(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
+  const int sub = threadIdx.x & 15;
+  if (item >= items) return;  // items is even per warp half; whole half-warps leave together
+  const long tok = item / H;
+  const int h = int(item % H);
+  const int col = h * 128 + sub * 8;
+  const uint4 x = *reinterpret_cast<const uint4*>(o + tok * ld_o + col);
+  const uint4 y = *reinterpret_cast<const uint4*>(dout + tok * ld_do + col);
+  const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 a = unpack_bf16x2(xs[k]), b = unpack_bf16x2(ys[k]);
+    s += a.x * b.x + a.y * b.y;
+  }
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  float4* q = reinterpret_cast<float4*>(dq_acc + tok * C + col);
+  q[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+  q[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (sub == 0) {
+    const long b = tok / T, t = tok % T;
+    dsum[(b * H + h) * T + t] = s;
+  }
+}
+
 void flash_bwd_prep(torch::Tensor out, torch::Tensor dout, torch::Tensor dsum, torch::Tensor dq_acc, int64_t B,
                     int64_t T, int64_t H) {
-  TORCH_CHECK(dq_acc.scalar_type() == at::kFloat && dq_acc.is_contiguous() && dq_acc.numel() == B * T * out.size(1),
+  const int64_t C = out.size(1);
+  TORCH_CHECK(dq_acc.scalar_type() == at::kFloat && dq_acc.is_contiguous() && dq_acc.numel() == B * T * C,
               "flash_bwd_prep: dq_acc");
+  TORCH_CHECK(C == H * 128 && out.scalar_type() == at::kBFloat16 && dout.scalar_type() == at::kBFloat16 &&
+                  out.stride(1) == 1 && dout.stride(1) == 1 && out.stride(0) % 8 == 0 && dout.stride(0) % 8 == 0 &&
+                  reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(dout.data_ptr()) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(dq_acc.data_ptr()) % 16 == 0,
+              "flash_bwd_prep: head_dim 128, 16-byte aligned rows");
+  TORCH_CHECK(dsum.scalar_type() == at::kFloat && dsum.numel() == B * H * T, "flash_bwd_prep: dsum");
   const at::cuda::CUDAGuard guard(out.device());
-  flash_dsum(out, dout, dsum, B, T, H);
-  TORCH_CHECK(cudaMemsetAsync(dq_acc.data_ptr(), 0, size_t(dq_acc.numel()) * 4, at::cuda::getCurrentCUDAStream()) ==
-                  cudaSuccess,
-              "flash_bwd_prep: memset");
+  const long items = B * T * H;
+  flash_bwd_prep_kernel<<<unsigned((items * 16 + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()), out.stride(0),
+      reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), dout.stride(0), dsum.data_ptr<float>(),
+      dq_acc.data_ptr<float>(), items, int(T), int(H), int(C));
+  TORCH_CHECK(cudaGetLastError() == cudaSuccess, "flash_bwd_prep launch failed");
 }
 
 // Full backward with the tcgen05 kernel: D precompute and zeroed fp32 dQ
@@ -602,11 +646,7 @@ void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torc
                   reinterpret_cast<uintptr_t>(dsum.data_ptr()) % 16 == 0, "flash_bwd_tc: 16-byte aligned lse/dsum");
   const at::cuda::CUDAGuard guard(qkv.device());
   auto stream = at::cuda::getCurrentCUDAStream();
-  if (!prepared) {
-    flash_dsum(out, dout, dsum, B, T, H);
-    TORCH_CHECK(cudaMemsetAsync(dq_acc.data_ptr(), 0, size_t(B * T * C) * 4, stream) == cudaSuccess,
-                "flash_bwd_tc: memset");
-  }
+  if (!prepared) flash_bwd_prep(out, dout, dsum, dq_acc, B, T, H);
   CUtensorMap tm = seq_map_3d(qkv.data_ptr(), B, T, 3 * C);
   CUtensorMap tmo = seq_map_3d(dout.data_ptr(), B, T, C);
   CUtensorMap tmq;
