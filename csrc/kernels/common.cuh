@@ -356,6 +356,11 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr, uint32_t lbo_
   return d;
 }
 
+// The same descriptor for a tile `bytes` further on (16-byte aligned; the start
+// address field holds addr >> 4 in 14 bits, which shared-memory addresses
+// below 256 KB never overflow): one 64-bit add instead of rebuilding it.
+__device__ __forceinline__ uint64_t desc_advance(uint64_t desc, uint32_t bytes) { return desc + (bytes >> 4); }
+
 // Instruction descriptor, kind::f16 with bf16 A/B and fp32 D.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn_major, bool b_mn_major) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(a_mn_major) << 15) | (uint32_t(b_mn_major) << 16) |

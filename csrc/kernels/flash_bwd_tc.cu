@@ -96,10 +96,14 @@ struct FbArgs {
 // 9 math done, 10 P^T stored to tensor memory, 11 dS^T stored to shared memory.
 __device__ long long g_fb_trace[64 * 16];
 
+template <bool DBG>
 __device__ __forceinline__ void fb_stamp(const FbArgs& a, int n, int k) {
-  if ((a.dbg & 512) && blockIdx.x == 0 && blockIdx.y == 0 && n < 64) g_fb_trace[n * 16 + k] = clock64();
+  if (DBG && (DBG && (a.dbg & 512)) && blockIdx.x == 0 && blockIdx.y == 0 && n < 64) g_fb_trace[n * 16 + k] = clock64();
 }
 
+// DBG: the build with the measurement switches (NANOGPT_FB_DEBUG); the
+// production instantiation carries none of their code.
+template <bool DBG>
 __global__ void __launch_bounds__(fb::kThreads, 1)
     flash_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tmo,
                         const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmd,
@@ -175,7 +179,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       for (int n = 0; n < nblk; ++n) {
         const int j = j0 + n, st = n % NS;
         if (!mbar_wait(&qd_empty[st], ((n / NS) & 1) ^ 1, kErrTimeoutProducer, a.err)) break;
-        if ((a.dbg & 128) && n >= NS) {
+        if ((DBG && (a.dbg & 128)) && n >= NS) {
           mbar_arrive(&qd_full[st]);
           continue;
         }
@@ -195,28 +199,33 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       const uint32_t id_kn = idesc_bf16(128, HD, false, true);  // dV, dK: B MN-major
       const uint32_t id_q = idesc_bf16(128, BQ, true, true);    // dQ^T: A and B MN-major
       const uint32_t k = smem_u32(sK), v = smem_u32(sV);
+      // Base descriptors; every operand below is one of these plus a constant offset.
+      const uint64_t dk_km = sw128_desc(k, 16, 1024), dv_km = sw128_desc(v, 16, 1024);
+      const uint64_t dk_mn = sw128_desc(k, kKSub, 1024);
+      const uint64_t dq_km = sw128_desc(smem_u32(sQ), 16, 1024), do_km = sw128_desc(smem_u32(sO), 16, 1024);
+      const uint64_t dq_mn = sw128_desc(smem_u32(sQ), kQSub, 1024), do_mn = sw128_desc(smem_u32(sO), kQSub, 1024);
+      const uint64_t dds_km = sw128_desc(smem_u32(sDs), 16, 1024), dds_mn = sw128_desc(smem_u32(sDs), kDsTile, 1024);
       // Scores of block n into buffer n & 1.
       auto scores = [&](int n) -> bool {
         const int st = n % NS, u = n & 1;
         if (!mbar_wait(&qd_full[st], (n / NS) & 1, kErrTimeoutMma, a.err)) return false;
         tc_fence_after();
-        const uint32_t q = smem_u32(sQ + st * kQTile), o = smem_u32(sO + st * kQTile);
+        const uint32_t qs = st * kQTile;
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
-          if (a.dbg & 16) break;
+          if (DBG && (a.dbg & 16)) break;
           const uint32_t ka = (kk >> 2) * kKSub + (kk & 3) * 32, qa = (kk >> 2) * kQSub + (kk & 3) * 32;
-          umma_bf16(tmem + 64 * u, sw128_desc(k + ka, 16, 1024), sw128_desc(q + qa, 16, 1024), id_s, kk > 0);
+          umma_bf16(tmem + 64 * u, desc_advance(dk_km, ka), desc_advance(dq_km, qs + qa), id_s, kk > 0);
         }
         // dP^T reuses the columns of dQ^T of block n - 2: wait until it was drained.
-        if (n >= 2 && !(a.dbg & 32) && !mbar_wait(&dq_free[u], ((n - 2) >> 1) & 1, kErrTimeoutMma, a.err))
+        if (n >= 2 && !(DBG && (a.dbg & 32)) && !mbar_wait(&dq_free[u], ((n - 2) >> 1) & 1, kErrTimeoutMma, a.err))
           return false;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
-          if (a.dbg & 16) break;
+          if (DBG && (a.dbg & 16)) break;
           const uint32_t ka = (kk >> 2) * kKSub + (kk & 3) * 32, qa = (kk >> 2) * kQSub + (kk & 3) * 32;
-          umma_bf16(tmem + 128 + 64 * u, sw128_desc(v + ka, 16, 1024), sw128_desc(o + qa, 16, 1024), id_s,
-                    kk > 0);
+          umma_bf16(tmem + 128 + 64 * u, desc_advance(dv_km, ka), desc_advance(do_km, qs + qa), id_s, kk > 0);
         }
         umma_commit(&st_full[u]);
         return true;
@@ -225,28 +234,27 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       for (int n = 0; n < nblk && ok; ++n) {
         const int st = n % NS, u = n & 1;
         if (n + 1 < nblk && !scores(n + 1)) break;
-        fb_stamp(a, n, 0);
-        if (!(a.dbg & 16384) && !mbar_wait(&p_full[u], (n >> 1) & 1, kErrTimeoutMma, a.err)) break;
-        fb_stamp(a, n, 1);
+        fb_stamp<DBG>(a, n, 0);
+        if (!(DBG && (a.dbg & 16384)) && !mbar_wait(&p_full[u], (n >> 1) & 1, kErrTimeoutMma, a.err)) break;
+        fb_stamp<DBG>(a, n, 1);
         tc_fence_after();
-        const uint32_t q = smem_u32(sQ + st * kQTile), o = smem_u32(sO + st * kQTile);
-        const uint32_t ds = smem_u32(sDs + u * kDsTile);
+        const uint32_t qs = st * kQTile, dss = u * kDsTile;
 #pragma unroll
-        for (int kk = 0; kk < BK / 16 && !(a.dbg & 4); ++kk)  // dQ^T = K^T dS^T: contraction over the 128 keys
-          umma_bf16(tmem + 128 + 64 * u, sw128_desc(k + kk * 2048, kKSub, 1024),
-                    sw128_desc(ds + kk * 2048, kDsTile, 1024), id_q, kk > 0);
+        for (int kk = 0; kk < BK / 16 && !(DBG && (a.dbg & 4)); ++kk)  // dQ^T = K^T dS^T: contraction over the 128 keys
+          umma_bf16(tmem + 128 + 64 * u, desc_advance(dk_mn, kk * 2048), desc_advance(dds_mn, dss + kk * 2048), id_q,
+                    kk > 0);
         umma_commit(&dq_full[u]);
 #pragma unroll
-        for (int kk = 0; kk < BQ / 16 && !(a.dbg & 8); ++kk) {  // contraction over the 64 queries
+        for (int kk = 0; kk < BQ / 16 && !(DBG && (a.dbg & 8)); ++kk) {  // contraction over the 64 queries
           // P^T is in tensor memory: 32 query columns of chunk c packed as bf16
           // pairs in TMEM columns [64u + 32c, 64u + 32c + 16) (written over S^T).
-          umma_bf16_ts(tmem + 384, tmem + 64 * u + 32 * (kk >> 1) + 8 * (kk & 1),
-                       sw128_desc(o + kk * 2048, kQSub, 1024), id_kn, (n > 0 || kk > 0) ? 1u : 0u);
-          umma_bf16(tmem + 256, sw128_desc(ds + kk * 32, 16, 1024), sw128_desc(q + kk * 2048, kQSub, 1024), id_kn,
+          umma_bf16_ts(tmem + 384, tmem + 64 * u + 32 * (kk >> 1) + 8 * (kk & 1), desc_advance(do_mn, qs + kk * 2048),
+                       id_kn, (n > 0 || kk > 0) ? 1u : 0u);
+          umma_bf16(tmem + 256, desc_advance(dds_km, dss + kk * 32), desc_advance(dq_mn, qs + kk * 2048), id_kn,
                     (n > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&qd_empty[st]);  // Q_j / dO_j / their LSE and D rows are no longer read
-        fb_stamp(a, n, 2);
+        fb_stamp<DBG>(a, n, 2);
       }
       umma_commit(kv_done);
     }
@@ -280,7 +288,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       // st_full of block n is committed after every MMA of block n - 2, so
       // dS^T tile u (read by dK / dQ of block n - 2) is free as well.
       if (!mbar_wait(&st_full[u], (n >> 1) & 1, kErrTimeoutEpilogue, a.err)) { ok = false; break; }
-      if (warp == 2 && lane == 0) fb_stamp(a, n, 3);
+      if (warp == 2 && lane == 0) fb_stamp<DBG>(a, n, 3);
       tc_fence_after();
       const bool diag = n < BK / BQ;
       const int q0 = j * BQ + 32 * half;
@@ -293,7 +301,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
         tmem_ld_32x16_issue(tmem + lanes + 128 + 64 * u + 32 * half + 16 * hh, dr);
         tmem_ld_wait16(sr);
         tmem_ld_wait16(dr);
-        if (warp == 2 && lane == 0 && hh == 0) fb_stamp(a, n, 8);
+        if (warp == 2 && lane == 0 && hh == 0) fb_stamp<DBG>(a, n, 8);
 #pragma unroll
         for (int i = 0; i < 16; i += 2) {
           float pv[2], gv[2];
@@ -308,9 +316,9 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
           dd[(16 * hh + i) / 2] = pack_bf16x2(gv[0], gv[1]);
         }
       }
-      if (warp == 2 && lane == 0) fb_stamp(a, n, 9);
+      if (warp == 2 && lane == 0) fb_stamp<DBG>(a, n, 9);
       tmem_st_32x16(tmem + lanes + 64 * u + 32 * half, pp);
-      if (warp == 2 && lane == 0) fb_stamp(a, n, 10);
+      if (warp == 2 && lane == 0) fb_stamp<DBG>(a, n, 10);
       uint8_t* ds = sDs + u * kDsTile;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {  // 16-byte chunk 4 * half + c of row r, 128-byte swizzle
@@ -318,14 +326,14 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
         *reinterpret_cast<uint4*>(ds + r * 128 + ((cc ^ (r & 7)) << 4)) =
             make_uint4(dd[4 * c], dd[4 * c + 1], dd[4 * c + 2], dd[4 * c + 3]);
       }
-      if (warp == 2 && lane == 0) fb_stamp(a, n, 11);
+      if (warp == 2 && lane == 0) fb_stamp<DBG>(a, n, 11);
       fence_proxy_async();
       tc_fence_before();
       __syncwarp();
-      if (warp == 2 && lane == 0) fb_stamp(a, n, 4);
+      if (warp == 2 && lane == 0) fb_stamp<DBG>(a, n, 4);
       if (lane == 0) mbar_arrive(&p_full[u]);
     }
-    if (ok && mbar_wait(kv_done, 0, kErrTimeoutEpilogue, a.err) && !(a.dbg & 256) &&
+    if (ok && mbar_wait(kv_done, 0, kErrTimeoutEpilogue, a.err) && !(DBG && (a.dbg & 256)) &&
         NK_IN_BOUNDS(key < a.T && b < a.B && h < a.H, a.err)) {
       tc_fence_after();
       // dK (warps of chunk 0) and dV (chunk 1) are staged as bf16 tiles in
@@ -452,7 +460,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
     for (int n = 0; n < nblk; ++n) {
       const int j = j0 + n, u = n & 1;
       if (!mbar_wait(&dq_full[u], (n >> 1) & 1, kErrTimeoutEpilogue, a.err)) break;
-      if (warp == 10 && lane == 0) fb_stamp(a, n, 5);
+      if (warp == 10 && lane == 0) fb_stamp<DBG>(a, n, 5);
       tc_fence_after();
       uint32_t xr[2][32];
       tmem_ld_32x32_issue(tmem + lanes + 128 + 64 * u, xr[0]);
@@ -463,9 +471,9 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&dq_free[u]);
-      if (warp == 10 && lane == 0) fb_stamp(a, n, 6);
-      if (a.dbg & 1) continue;
-      if (a.dbg & 8192) {  // measurement: coalesced red.global.add from registers, no staging
+      if (warp == 10 && lane == 0) fb_stamp<DBG>(a, n, 6);
+      if (DBG && (a.dbg & 1)) continue;
+      if (DBG && (a.dbg & 8192)) {  // measurement: coalesced red.global.add from registers, no staging
         float* dst = a.dq_acc + (long(b) * a.T + j * BQ) * a.C + h * HD + quarter * 32 + lane;
 #pragma unroll
         for (int c = 0; c < 2; ++c)
@@ -684,13 +692,17 @@ void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torc
   }
   static bool configured = false;
   if (!configured) {
-    TORCH_CHECK(cudaFuncSetAttribute(flash_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) ==
-                    cudaSuccess, "flash_bwd_tc: smem");
+    TORCH_CHECK(cudaFuncSetAttribute(flash_bwd_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmem) == cudaSuccess &&
+                    cudaFuncSetAttribute(flash_bwd_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kSmem) == cudaSuccess,
+                "flash_bwd_tc: smem");
     configured = true;
   }
   dim3 grid(unsigned(T / BK), unsigned(B * H));
   CUtensorMap tmd = seq_map_3d(dqkv.data_ptr(), B, T, 3 * C);
-  flash_bwd_tc_kernel<<<grid, kThreads, kSmem, stream>>>(tm, tmo, tmq, tmd, a);
+  if (a.dbg) flash_bwd_tc_kernel<true><<<grid, kThreads, kSmem, stream>>>(tm, tmo, tmq, tmd, a);
+  else flash_bwd_tc_kernel<false><<<grid, kThreads, kSmem, stream>>>(tm, tmo, tmq, tmd, a);
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "flash_bwd_tc launch failed");
   const long items = B * T * H;
   dq_finish_kernel<<<unsigned((items + 7) / 8), 256, 0, stream>>>(a.dq_acc, a.dqkv, B * T, int(T), int(H), int(C),

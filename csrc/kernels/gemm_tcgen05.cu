@@ -304,6 +304,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_commit(bar);
         }
       };
+      // Operand descriptors of stage 0; a stage and a 16-deep K step are byte offsets on them.
+      const uint32_t sa0 = smem_u32(smem), sb0 = sa0 + S::kABytes;
+      const uint64_t a_desc0 = args.a_mn_major ? sw128_desc(sa0, 8192, 1024) : sw128_desc(sa0, 16, 1024);
+      const uint64_t b_desc0 = args.b_mn_major ? sw128_desc(sb0, 8192, 1024) : sw128_desc(sb0, 16, 1024);
+      const uint32_t a_kstep = args.a_mn_major ? 2048 : 32, b_kstep = args.b_mn_major ? 2048 : 32;
       long long w_acc = 0, w_ld = 0;
       const long long t_begin = clock64();
       for (int u = cta_id; u < units && ok; u += n_ctas, ++local) {
@@ -321,14 +326,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait(&full_bar[stage], phase, kErrTimeoutMma, args.err)) { ok = false; break; }
           if (args.trace) w_ld += clock64() - t0;
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + stage * S::kStageBytes);
-          const uint32_t sb = sa + S::kABytes;
+          const uint32_t so = stage * S::kStageBytes;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t ad = args.a_mn_major ? sw128_desc(sa + k * 2048, 8192, 1024)
-                                                : sw128_desc(sa + k * 32, 16, 1024);
-            const uint64_t bd = args.b_mn_major ? sw128_desc(sb + k * 2048, 8192, 1024)
-                                                : sw128_desc(sb + k * 32, 16, 1024);
+            const uint64_t ad = desc_advance(a_desc0, so + k * a_kstep);
+            const uint64_t bd = desc_advance(b_desc0, so + k * b_kstep);
             if (PAIR) umma_bf16_pair(d_tmem, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
             else umma_bf16(d_tmem, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
