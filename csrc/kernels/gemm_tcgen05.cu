@@ -370,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) {
         mbar_arrive_expect_tx(&aux_bar[2 * ew + (ckk & 1)], kStageBufBytes);
-        if (NK_IN_BOUNDS(col % 8 == 0 && col >= 0 && col < args.N && row >= 0 && row < args.M + BM, args.err))
+        if (NK_IN_BOUNDS(col % 8 == 0 && col >= 0 && col < args.N && row >= 0 && row < args.M + kTileM, args.err))
           tma_load_2d(bufX(ckk), &tmX, &aux_bar[2 * ew + (ckk & 1)], col, row);
       }
     };
@@ -433,7 +433,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_proxy_async();
           __syncwarp();
           if (lane == 0) {
-            if (NK_IN_BOUNDS(row0 >= 0 && row0 < args.M + BM && colb + c4 * 32 < args.N, args.err))
+            // A pair's second CTA can hold only rows past M in the last tile row: nothing to store.
+            if (row0 < args.M && NK_IN_BOUNDS(row0 >= 0 && colb + c4 * 32 < args.N, args.err))
               tma_store_2d(&tmC, sb, colb + c4 * 32, row0);
             bulk_commit();
           }
@@ -523,7 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) {
           // (Rows past M inside the last tile are clipped by the TMA store.)
-          if (NK_IN_BOUNDS(col0 % 8 == 0 && col0 >= 0 && col0 < args.N && row0 >= 0 && row0 < args.M + BM, args.err)) {
+          if (row0 < args.M && NK_IN_BOUNDS(col0 % 8 == 0 && col0 >= 0 && col0 < args.N && row0 >= 0, args.err)) {
             tma_store_2d(&tmC, bufS(ck), col0, row0);
             if (keep_h) tma_store_2d(&tmX, bufX(ck), col0, row0);
           }
