@@ -68,17 +68,22 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
   uint8_t* sQ = smem;                       // 2 tiles
   uint8_t* sK = smem + 2 * kTileBytes;      // 2 buffers
   uint8_t* sV = smem + 4 * kTileBytes;
-  uint8_t* sP = smem + 5 * kTileBytes;      // 2 tiles
+  uint8_t* sP = smem + 5 * kTileBytes;      // 2 tiles (P staged in shared memory)
+  // With P in tensor memory the P region holds a second V buffer, so V_{j+1}
+  // streams in while P V_j runs (a single buffer put the V load's full
+  // latency between P_1 V_j and P_0 V_{j+1} on every key block).
+  constexpr int VB = P_TMEM ? 2 : 1;
+  auto v_buf = [&](int j) { return (VB == 2 && (j & 1)) ? sP : sV; };
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 7 * kTileBytes);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;   // [2]
   uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;
-  uint64_t* v_empty = bars + 6;
-  uint64_t* s_full = bars + 7;   // [2]
-  uint64_t* p_full = bars + 9;   // [2]
-  uint64_t* o_done = bars + 11;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t* v_full = bars + 5;   // [VB]
+  uint64_t* v_empty = bars + 7;  // [VB]
+  uint64_t* s_full = bars + 9;   // [2]
+  uint64_t* p_full = bars + 11;  // [2]
+  uint64_t* o_done = bars + 13;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int qb = gridDim.x - 1 - blockIdx.x;  // longest rows first
@@ -93,8 +98,10 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
     }
-    mbar_init(v_full, 1);
-    mbar_init(v_empty, 1);
+    for (int i = 0; i < VB; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
       mbar_init(&p_full[t], 4);
@@ -123,9 +130,10 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
         mbar_arrive_expect_tx(&k_full[kb], kTileBytes);
         for (int s = 0; s < 2; ++s)
           tma_load_3d(sK + kb * kTileBytes + s * kSubBytes, &tm, &k_full[kb], xk + 64 * s, j * BN, b);
-        if (!mbar_wait(v_empty, (j & 1) ^ 1, kErrTimeoutProducer, a.err)) break;
-        mbar_arrive_expect_tx(v_full, kTileBytes);
-        for (int s = 0; s < 2; ++s) tma_load_3d(sV + s * kSubBytes, &tm, v_full, xv + 64 * s, j * BN, b);
+        const int vb = j % VB;
+        if (!mbar_wait(&v_empty[vb], ((j / VB) & 1) ^ 1, kErrTimeoutProducer, a.err)) break;
+        mbar_arrive_expect_tx(&v_full[vb], kTileBytes);
+        for (int s = 0; s < 2; ++s) tma_load_3d(v_buf(j) + s * kSubBytes, &tm, &v_full[vb], xv + 64 * s, j * BN, b);
       }
     }
   } else if (warp == 1) {
@@ -147,7 +155,7 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
         umma_commit(&s_full[t]);
       };
       auto issue_pv = [&](int t, int j) {
-        const uint32_t p = smem_u32(sP + t * kTileBytes), v = smem_u32(sV);
+        const uint32_t p = smem_u32(sP + t * kTileBytes), v = smem_u32(v_buf(j));
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           if constexpr (P_TMEM) {
@@ -171,7 +179,7 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
       }
       for (int j = 0; j < nblk1 && ok; ++j) {
         const bool next = j + 1 < nblk1;  // tile 1 (and tile 0 if j + 1 < nblk0) has block j + 1
-        if (!mbar_wait(v_full, j & 1, kErrTimeoutMma, a.err)) break;
+        if (!mbar_wait(&v_full[j % VB], (j / VB) & 1, kErrTimeoutMma, a.err)) break;
         if (j < nblk0) {
           if (!mbar_wait(&p_full[0], j & 1, kErrTimeoutMma, a.err)) break;
           tc_fence_after();
@@ -183,7 +191,7 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
         if (!mbar_wait(&p_full[1], j & 1, kErrTimeoutMma, a.err)) break;
         tc_fence_after();
         issue_pv(1, j);
-        umma_commit(v_empty);
+        umma_commit(&v_empty[j % VB]);
         if (next) {
           issue_s(1, j + 1);
           umma_commit(&k_empty[(j + 1) & 1]);
@@ -218,9 +226,17 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
         for (int i = 0; i < BN; ++i)
           if (i > lim) sv[i] = -INFINITY;
       }
-      float mraw = sv[0];
+      // Row max over eight independent chains (one chain of 127 dependent
+      // max instructions would put its whole latency on the softmax path).
+      float mx8[8];
 #pragma unroll
-      for (int i = 1; i < BN; ++i) mraw = fmaxf(mraw, sv[i]);
+      for (int k = 0; k < 8; ++k) mx8[k] = sv[k];
+#pragma unroll
+      for (int i = 8; i < BN; i += 8)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(mx8[k], sv[i + k]);
+      const float mraw = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float mx = mraw * a.sl2;  // sl2 > 0: max commutes with the scale
       // The previous P V must be done before P is rewritten or O rescaled.
       if (j > 0 && !mbar_wait(&o_done[t], (j - 1) & 1, kErrTimeoutEpilogue, a.err)) { ok = false; break; }
@@ -243,7 +259,7 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
         m_used = m_new;
       }
       // P = exp2(s - m_used) -> bf16 in shared memory.
-      float rs = 0.f;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};  // four independent partial sums
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t pk[16];
@@ -251,7 +267,7 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
         for (int i = 0; i < 32; i += 2) {
           const float p0 = ex2_approx(fmaf(sv[c * 32 + i], a.sl2, -m_used));
           const float p1 = ex2_approx(fmaf(sv[c * 32 + i + 1], a.sl2, -m_used));
-          rs += p0 + p1;
+          rs4[(i >> 1) & 3] += p0 + p1;
           pk[i / 2] = pack_bf16x2(p0, p1);
         }
         if constexpr (P_TMEM) {
@@ -264,7 +280,7 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
                                                                              pk[4 * q + 3]);
         }
       }
-      l += rs;
+      l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
       fence_proxy_async();  // generic-proxy smem writes -> visible to the tensor core
       tc_fence_before();
       __syncwarp();

@@ -619,6 +619,16 @@ static int pair_mode() {
   return mode;
 }
 
+// NANOGPT_GEMM_BALANCE=0 keeps the caller's split count for the split-K
+// weight gradients (measurement switch).
+static int balance_mode() {
+  static const int mode = [] {
+    const char* e = std::getenv("NANOGPT_GEMM_BALANCE");
+    return e ? std::atoi(e) : 1;
+  }();
+  return mode;
+}
+
 // NANOGPT_GEMM_ROTATE=0 keeps one staging buffer per output chunk (A/B switch).
 static int rotate_mode() {
   static const int mode = [] {
@@ -706,6 +716,20 @@ void gemm_impl(torch::Tensor A, bool a_mn_major, torch::Tensor B, bool b_mn_majo
   args.num_n = (N + BN - 1) / BN;
   args.kb_total = (K + BK - 1) / BK;
   int s = int(std::max<int64_t>(1, std::min<int64_t>(splits, args.kb_total)));
+  if (mode == kAtomicF32 && s > 1 && balance_mode()) {
+    // Split-K weight gradients: among s .. 2s splits take the one whose last
+    // round of units leaves the fewest CTAs idle; per-CTA time is modelled as
+    // rounds x (k-blocks per unit + 2 for the unit's pipeline fill and flush).
+    const long n_ctas = pair ? num_sms() / 2 : num_sms(), tiles = long(args.num_m) * args.num_n;
+    long best = -1;
+    int best_s = s;
+    for (int c = s; c <= 2 * s && c <= args.kb_total; ++c) {
+      const long kps = (args.kb_total + c - 1) / c, units = tiles * ((args.kb_total + kps - 1) / kps);
+      const long cost = ((units + n_ctas - 1) / n_ctas) * (kps + 2);
+      if (best < 0 || cost < best) { best = cost; best_s = c; }
+    }
+    s = best_s;
+  }
   args.kb_per_split = (args.kb_total + s - 1) / s;
   args.splits = (args.kb_total + args.kb_per_split - 1) / args.kb_per_split;
 
