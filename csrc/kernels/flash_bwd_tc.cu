@@ -510,42 +510,61 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
 }
 
 // dQ accumulator (fp32, (B*T, C)) -> bf16 q columns of dqkv, optionally
-// through the RoPE + QK-norm backward. One warp per (token, head); lane l
-// owns elements [4l, 4l+4), its rotation partners live in lane l ^ 16.
+// through the RoPE + QK-norm backward. A warp handles kDqItems (token, head)
+// items, issuing all their loads before any arithmetic so several rows'
+// memory latencies overlap; in an item lane l owns elements [4l, 4l+4), its
+// rotation partners live in lane l ^ 16.
+constexpr int kDqItems = 4;
 __global__ void dq_finish_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dqkv, long rows, int T,
                                  int H, int C, const __nv_bfloat16* __restrict__ qkv, const float* __restrict__ rstd,
                                  const float* __restrict__ cos_t, const float* __restrict__ sin_t) {
-  const long item = long(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+  const long item0 = (long(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32) * kDqItems;
   const int lane = threadIdx.x & 31;
-  if (item >= rows * H) return;
-  const long row = item / H;
-  const int h = int(item % H);
-  const float4 g4 = *reinterpret_cast<const float4*>(acc + row * C + h * 128 + lane * 4);
-  float g[4] = {g4.x, g4.y, g4.z, g4.w};
-  if (rstd) {
-    const uint2 w = *reinterpret_cast<const uint2*>(qkv + row * 3 * C + h * 128 + lane * 4);
-    const float2 y0 = unpack_bf16x2(w.x), y1 = unpack_bf16x2(w.y);
-    const float y[4] = {y0.x, y0.y, y1.x, y1.y};
-    float dot = y[0] * g[0] + y[1] * g[1] + y[2] * g[2] + y[3] * g[3];
+  const long items = rows * H;
+  float4 g4[kDqItems];
+  uint2 yw[kDqItems];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-    dot /= 128.f;
-    const float r = rstd[row * 2 * H + h];
-    const int pos = int(row % T);
-    float dr[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) dr[j] = r * (g[j] - y[j] * dot);
-    const bool first = lane < 16;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float partner = __shfl_xor_sync(0xffffffffu, dr[j], 16);
-      const int i = (lane & 15) * 4 + j;
-      const float cs = cos_t[pos * 64 + i], sn = sin_t[pos * 64 + i];
-      g[j] = first ? dr[j] * cs - partner * sn : partner * sn + dr[j] * cs;
+  for (int k = 0; k < kDqItems; ++k) {
+    const long item = item0 + k;
+    if (item < items) {
+      const long row = item / H;
+      const int h = int(item % H);
+      g4[k] = *reinterpret_cast<const float4*>(acc + row * C + h * 128 + lane * 4);
+      if (rstd) yw[k] = *reinterpret_cast<const uint2*>(qkv + row * 3 * C + h * 128 + lane * 4);
     }
   }
-  *reinterpret_cast<uint2*>(dqkv + row * 3 * C + h * 128 + lane * 4) =
-      make_uint2(pack_bf16x2(g[0], g[1]), pack_bf16x2(g[2], g[3]));
+#pragma unroll
+  for (int k = 0; k < kDqItems; ++k) {
+    const long item = item0 + k;
+    if (item >= items) break;  // uniform across the warp
+    const long row = item / H;
+    const int h = int(item % H);
+    float g[4] = {g4[k].x, g4[k].y, g4[k].z, g4[k].w};
+    if (rstd) {
+      const float2 y0 = unpack_bf16x2(yw[k].x), y1 = unpack_bf16x2(yw[k].y);
+      const float y[4] = {y0.x, y0.y, y1.x, y1.y};
+      float dot = y[0] * g[0] + y[1] * g[1] + y[2] * g[2] + y[3] * g[3];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      dot /= 128.f;
+      const float r = rstd[row * 2 * H + h];
+      const int pos = int(row % T);
+      float dr[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) dr[j] = r * (g[j] - y[j] * dot);
+      const bool first = lane < 16;
+      const float4 cs4 = *reinterpret_cast<const float4*>(cos_t + pos * 64 + (lane & 15) * 4);
+      const float4 sn4 = *reinterpret_cast<const float4*>(sin_t + pos * 64 + (lane & 15) * 4);
+      const float cs[4] = {cs4.x, cs4.y, cs4.z, cs4.w}, sn[4] = {sn4.x, sn4.y, sn4.z, sn4.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float partner = __shfl_xor_sync(0xffffffffu, dr[j], 16);
+        g[j] = first ? dr[j] * cs[j] - partner * sn[j] : partner * sn[j] + dr[j] * cs[j];
+      }
+    }
+    *reinterpret_cast<uint2*>(dqkv + row * 3 * C + h * 128 + lane * 4) =
+        make_uint2(pack_bf16x2(g[0], g[1]), pack_bf16x2(g[2], g[3]));
+  }
 }
 
 // The timeline written under NANOGPT_FB_DEBUG bit 9 (see g_fb_trace).
@@ -705,7 +724,7 @@ void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torc
   else flash_bwd_tc_kernel<false><<<grid, kThreads, kSmem, stream>>>(tm, tmo, tmq, tmd, a);
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "flash_bwd_tc launch failed");
   const long items = B * T * H;
-  dq_finish_kernel<<<unsigned((items + 7) / 8), 256, 0, stream>>>(a.dq_acc, a.dqkv, B * T, int(T), int(H), int(C),
+  dq_finish_kernel<<<unsigned((items + 8 * kDqItems - 1) / (8 * kDqItems)), 256, 0, stream>>>(a.dq_acc, a.dqkv, B * T, int(T), int(H), int(C),
                                                                 a.qkv, a.rope_rstd, a.rope_cos, a.rope_sin);
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "dq_finish launch failed");
 }
