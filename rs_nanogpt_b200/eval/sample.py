@@ -26,7 +26,7 @@ class SampleOptions:
 
 
 def argmax(logits: np.ndarray) -> int:
-    # First index of the maximum, with NaN treated as largest (total order).
+    # Last index of the maximum (ties go to the later id), with NaN treated as largest (total order).
     if np.isnan(logits).any():
         return int(np.flatnonzero(np.isnan(logits))[-1])
     m = logits.max()
