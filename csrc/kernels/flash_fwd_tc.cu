@@ -51,6 +51,7 @@ struct FaArgs {
   int B, H, T, C;
   float sl2;
   int* err;
+  int st_defer;  // P stores to tensor memory waited for once per block (NANOGPT_FWD_ST_DEFER, default 1)
 };
 
 // P tile staging: row r, 16-byte chunk c (8 keys) of the 128 keys; sub-tile
@@ -271,8 +272,10 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
           pk[i / 2] = pack_bf16x2(p0, p1);
         }
         if constexpr (P_TMEM) {
-          // Over this row's own S columns, all of which are already in registers.
-          tmem_st_32x16(t_s + 16 * c, pk);
+          // Over this row's own S columns, all of which are already in registers;
+          // the four stores overlap the next chunks' math and are waited for once.
+          if (a.st_defer) tmem_st_32x16_issue(t_s + 16 * c, pk);
+          else tmem_st_32x16(t_s + 16 * c, pk);
         } else {
 #pragma unroll
           for (int q = 0; q < 4; ++q)
@@ -281,7 +284,12 @@ __global__ void __launch_bounds__(fa::kThreads, 1)
         }
       }
       l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
-      fence_proxy_async();  // generic-proxy smem writes -> visible to the tensor core
+      if constexpr (P_TMEM) {
+        if (a.st_defer) tmem_st_wait();
+      } else {
+        fence_proxy_async();
+      }
+      // (shared-memory P: the proxy fence makes the generic writes visible to the tensor core)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t]);
@@ -341,6 +349,11 @@ void flash_fwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor lse, int64
   a.B = int(B); a.H = int(H); a.T = int(T); a.C = int(C);
   a.sl2 = (1.f / std::sqrt(float(HD))) * 1.4426950408889634f;
   a.err = error_word();
+  static const int st_defer = [] {
+    const char* e = std::getenv("NANOGPT_FWD_ST_DEFER");
+    return e ? std::atoi(e) : 1;
+  }();
+  a.st_defer = st_defer;
   static const int p_tmem = [] {
     const char* e = std::getenv("NANOGPT_FWD_P_TMEM");
     return e ? std::atoi(e) : 1;
