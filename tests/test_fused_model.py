@@ -71,3 +71,29 @@ def test_qkv_gemm_with_fused_rope_matches_separate_kernels():
     gemm.linear_qkv_rope(x, w, out, r2, cos.t().contiguous(), sin.t().contiguous(), 256, 2, 1e-6)
     assert (out.float() - ref.float()).abs().max().item() < 3e-2
     assert (r1 - r2).abs().max().item() < 1e-3 * r1.abs().max().item()
+
+
+def test_qkv_gemm_with_fused_rope_matches_the_fp32_oracle():
+    """The QKV GEMM's RoPE + QK-RMSNorm epilogue against the fp32 model math
+    (models/reference.py: projection, apply_rope, rms_norm per head)."""
+    from rs_nanogpt_b200.config import GptConfig
+    from rs_nanogpt_b200.models.reference import apply_rope, rms_norm, rope_tables
+    from rs_nanogpt_b200.ops import gemm
+    torch.manual_seed(4)
+    b, t, nh, hd = 2, 256, 2, 128
+    c = nh * hd
+    cfg = GptConfig(sequence_len=t, n_head=nh, n_embd=c, rope_base=10000.0)
+    cos, sin = rope_tables(cfg, "cuda")
+    x = torch.randn(b * t, c, device="cuda").bfloat16()
+    w = (torch.randn(3 * c, c, device="cuda") * 0.05).bfloat16()
+    out = torch.empty(b * t, 3 * c, device="cuda", dtype=torch.bfloat16)
+    rstd = torch.empty(b * t * 2 * nh, device="cuda")
+    gemm.linear_qkv_rope(x, w, out, rstd, cos.t().contiguous(), sin.t().contiguous(), t, nh, 1e-6)
+    y = x.float() @ w.float().t()
+    heads = lambda z: z.view(b, t, nh, hd).transpose(1, 2)
+    q = rms_norm(apply_rope(heads(y[:, :c]), cos.float(), sin.float(), 0), 1e-6)
+    k = rms_norm(apply_rope(heads(y[:, c:2 * c]), cos.float(), sin.float(), 0), 1e-6)
+    got = out.float()
+    for ref, part in ((q, got[:, :c]), (k, got[:, c:2 * c])):
+        assert (heads(part) - ref).abs().max().item() < 3e-2
+    assert (got[:, 2 * c:] - y[:, 2 * c:]).abs().max().item() < 2e-2 * max(1.0, y.abs().max().item())
