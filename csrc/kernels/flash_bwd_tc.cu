@@ -86,6 +86,7 @@ struct FbArgs {
   // adds dQ with red.global.add from registers instead of TMA reduce-adds, bit 14
   // makes the MMA warp skip its wait for the softmax warps.
   int dbg;
+  int st_defer;  // NANOGPT_BWD_ST_DEFER (default 1): see the P^T store in the softmax-gradient warps
 };
 
 // Timeline of the first CTA (measurement switch NANOGPT_FB_DEBUG bit 9): per
@@ -317,7 +318,10 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
         }
       }
       if (warp == 2 && lane == 0) fb_stamp<DBG>(a, n, 9);
-      tmem_st_32x16(tmem + lanes + 64 * u + 32 * half, pp);
+      // P^T to tensor memory; with st_defer its completion is awaited after the
+      // dS^T shared-memory stores below, so the two overlap.
+      if (a.st_defer) tmem_st_32x16_issue(tmem + lanes + 64 * u + 32 * half, pp);
+      else tmem_st_32x16(tmem + lanes + 64 * u + 32 * half, pp);
       if (warp == 2 && lane == 0) fb_stamp<DBG>(a, n, 10);
       uint8_t* ds = sDs + u * kDsTile;
 #pragma unroll
@@ -327,6 +331,7 @@ __global__ void __launch_bounds__(fb::kThreads, 1)
             make_uint4(dd[4 * c], dd[4 * c + 1], dd[4 * c + 2], dd[4 * c + 3]);
       }
       if (warp == 2 && lane == 0) fb_stamp<DBG>(a, n, 11);
+      if (a.st_defer) tmem_st_wait();
       fence_proxy_async();
       tc_fence_before();
       __syncwarp();
@@ -698,6 +703,11 @@ void flash_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torc
   a.sl2 = a.scale * 1.4426950408889634f;
   a.err = error_word();
   if (const char* d = std::getenv("NANOGPT_FB_DEBUG")) a.dbg = std::atoi(d);
+  static const int bwd_st_defer = [] {
+    const char* e = std::getenv("NANOGPT_BWD_ST_DEFER");
+    return e ? std::atoi(e) : 1;
+  }();
+  a.st_defer = bwd_st_defer;
   if (rope_rstd.has_value()) {
     TORCH_CHECK(rope_cos.has_value() && rope_sin.has_value() && rope_cos->size(1) == 64 && rope_cos->size(0) >= T &&
                     rope_cos->is_contiguous() && rope_sin->is_contiguous() &&
